@@ -1,0 +1,278 @@
+"""Host side of the batch-invariant GEMM: operand canonicalisation and launch.
+
+Everything here goes straight to ``bio_gemm`` / ``bio_pack_rows`` in the
+kernel library; no torch matmul is ever called (calling one from inside an
+``aten::mm`` override would re-enter the override).
+
+Operand rules of the tensor-core path (bf16/fp16): A is K-contiguous, B is K-
+or N-contiguous, base pointers and row/batch strides are 16-byte aligned.
+Operands that break a rule are first copied by ``bio_pack_rows`` into a dense
+K-contiguous buffer whose K is padded with zeros to a multiple of 8.  The copy
+is exact and the zero tail lies inside the last 64-wide K block that the
+kernel zero-fills anyway, so packing never changes a result bit.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+
+def _ceil8(x: int) -> int:
+    return (x + 7) // 8 * 8
+
+
+@dataclass
+class Operand:
+    """A [batch1][batch2/div2][rows][cols] operand description (element strides)."""
+
+    tensor: torch.Tensor  # keeps the storage alive for the launch
+    ptr: int
+    s_row: int
+    s_col: int
+    s1: int
+    s2: int
+    div2: int = 1
+
+
+# Placeholder operand for K == 0 (the library fills C with the bias and never
+# reads A or B).
+_EMPTY = Operand(None, 0, 1, 1, 0, 0, 1)
+
+
+def _aligned16(t: torch.Tensor) -> bool:
+    return t.data_ptr() % 16 == 0
+
+
+def _pack(
+    x: torch.Tensor,
+    nb1: int,
+    nb2: int,
+    rows: int,
+    cols: int,
+    s_b1: int,
+    s_b2: int,
+    s_row: int,
+    s_col: int,
+) -> tuple[torch.Tensor, int]:
+    """Dense [nb1, nb2, rows, cols_pad] copy of a strided operand."""
+    cols_pad = _ceil8(max(cols, 1))
+    out = torch.empty((nb1, nb2, rows, cols_pad), dtype=x.dtype, device=x.device)
+    lib = _lib.load()
+    _lib.check(
+        lib.bio_pack_rows(
+            _lib.DTYPE_CODE[x.dtype],
+            ctypes.c_void_p(x.data_ptr()),
+            nb1,
+            nb2,
+            rows,
+            cols,
+            s_b1,
+            s_b2,
+            s_row,
+            s_col,
+            ctypes.c_void_p(out.data_ptr()),
+            cols_pad,
+            x.device.index,
+            _lib.stream_of(x),
+        ),
+        "bio_pack_rows",
+    )
+    return out, cols_pad
+
+
+def operand_a(
+    x: torch.Tensor,
+    batch1: int,
+    batch2: int,
+    rows: int,
+    k: int,
+    s_row: int,
+    s_k: int,
+    s1: int,
+    s2: int,
+    div2: int = 1,
+) -> Operand:
+    """A operand (rows = M, cols = K) for the GEMM of ``x.dtype``."""
+    if batch1 <= 1:
+        s1 = 0 if batch1 == 1 else s1
+    if rows == 1:
+        s_row = _ceil8(k)
+    if k == 1:
+        s_k = 1
+    if x.dtype == torch.float32:
+        return Operand(x, x.data_ptr(), s_row, s_k, s1, s2, div2)
+    common = s1 % 8 == 0 and s2 % 8 == 0 and _aligned16(x)
+    if common and s_k == 1 and s_row % 8 == 0:
+        return Operand(x, x.data_ptr(), s_row, 1, s1, s2, div2)
+    if common and s_row == 1 and s_k % 8 == 0 and rows > 1:
+        return Operand(x, x.data_ptr(), 1, s_k, s1, s2, div2)
+    nb1 = 1 if s1 == 0 else batch1
+    nb2 = 1 if s2 == 0 else (batch2 + div2 - 1) // div2
+    packed, kp = _pack(x, nb1, nb2, rows, k, s1, s2, s_row, s_k)
+    return Operand(
+        packed,
+        packed.data_ptr(),
+        kp,
+        1,
+        0 if s1 == 0 else nb2 * rows * kp,
+        0 if s2 == 0 else rows * kp,
+        div2,
+    )
+
+
+def operand_b(
+    x: torch.Tensor,
+    batch1: int,
+    batch2: int,
+    k: int,
+    n: int,
+    s_k: int,
+    s_n: int,
+    s1: int,
+    s2: int,
+    div2: int = 1,
+) -> Operand:
+    """B operand: element (k, n) at s_k*k + s_n*n.  ``s_row``/``s_col`` of the
+    returned Operand are (s_k, s_n)."""
+    if batch1 <= 1:
+        s1 = 0 if batch1 == 1 else s1
+    if n == 1 and k == 1:
+        s_k, s_n = 1, 8
+    elif n == 1:
+        if s_k == 1:
+            s_n = _ceil8(k)
+    elif k == 1:
+        if s_n == 1:
+            s_k = _ceil8(n)
+    if x.dtype == torch.float32:
+        return Operand(x, x.data_ptr(), s_k, s_n, s1, s2, div2)
+    common = s1 % 8 == 0 and s2 % 8 == 0 and _aligned16(x)
+    if common and s_k == 1 and s_n % 8 == 0:
+        return Operand(x, x.data_ptr(), 1, s_n, s1, s2, div2)
+    if common and s_n == 1 and s_k % 8 == 0:
+        return Operand(x, x.data_ptr(), s_k, 1, s1, s2, div2)
+    nb1 = 1 if s1 == 0 else batch1
+    nb2 = 1 if s2 == 0 else (batch2 + div2 - 1) // div2
+    # pack as K-major: rows = n, cols = k
+    packed, kp = _pack(x, nb1, nb2, n, k, s1, s2, s_n, s_k)
+    return Operand(
+        packed,
+        packed.data_ptr(),
+        1,
+        kp,
+        0 if s1 == 0 else nb2 * n * kp,
+        0 if s2 == 0 else n * kp,
+        div2,
+    )
+
+
+def launch(
+    a: Operand,
+    b: Operand,
+    c: torch.Tensor,
+    *,
+    batch1: int,
+    batch2: int,
+    m: int,
+    n: int,
+    k: int,
+    c_sm: int,
+    c_sn: int,
+    c_s1: int,
+    c_s2: int,
+    bias: torch.Tensor | None = None,
+    bias_per_row: bool = False,
+    bias_s2: int = 0,
+    alpha: float = 1.0,
+) -> None:
+    """Enqueue one bio_gemm on the current stream of ``c``'s device."""
+    args = _lib.GemmArgs()
+    args.dtype = _lib.DTYPE_CODE[c.dtype]
+    args.flags = _lib.BIO_GEMM_BIAS_PER_ROW if bias_per_row else 0
+    args.batch1 = batch1
+    args.batch2 = batch2
+    args.m, args.n, args.k = m, n, k
+    args.a = a.ptr
+    args.a_sm, args.a_sk, args.a_s1, args.a_s2, args.a_div2 = (
+        a.s_row,
+        a.s_col,
+        a.s1,
+        a.s2,
+        a.div2,
+    )
+    args.b = b.ptr
+    args.b_sk, args.b_sn, args.b_s1, args.b_s2, args.b_div2 = (
+        b.s_row,
+        b.s_col,
+        b.s1,
+        b.s2,
+        b.div2,
+    )
+    args.c = c.data_ptr()
+    args.c_sm, args.c_sn, args.c_s1, args.c_s2 = c_sm, c_sn, c_s1, c_s2
+    args.bias = bias.data_ptr() if bias is not None else None
+    args.bias_s2 = bias_s2
+    args.alpha = alpha
+    args.device = c.device.index
+    _lib.check(_lib.load().bio_gemm(ctypes.byref(args), _lib.stream_of(c)), "bio_gemm")
+
+
+def mm(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """C[M,N] = A[M,K] @ B[K,N] (+ bias[N]); any strides."""
+    m, k = a.shape
+    n = b.shape[1]
+    c = torch.empty((m, n), device=a.device, dtype=a.dtype)
+    if m == 0 or n == 0:
+        return c
+    if bias is not None:
+        bias = bias.to(a.dtype).contiguous()
+    if k == 0:
+        opa = opb = _EMPTY
+    else:
+        opa = operand_a(a, 1, 1, m, k, a.stride(0), a.stride(1), 0, 0)
+        opb = operand_b(b, 1, 1, k, n, b.stride(0), b.stride(1), 0, 0)
+    launch(
+        opa, opb, c, batch1=1, batch2=1, m=m, n=n, k=k, c_sm=n, c_sn=1, c_s1=0, c_s2=0, bias=bias
+    )
+    return c
+
+
+def bmm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tensor:
+    """C[b] = A[b] @ B[b]; each batch element is an independent fixed-schedule GEMM."""
+    nb, m, k = a.shape
+    n = b.shape[2]
+    c = torch.empty((nb, m, n), device=a.device, dtype=a.dtype)
+    if nb == 0 or m == 0 or n == 0:
+        return c
+    if k == 0:
+        opa = opb = _EMPTY
+    else:
+        opa = operand_a(a, nb, 1, m, k, a.stride(1), a.stride(2), a.stride(0), 0)
+        opb = operand_b(b, nb, 1, k, n, b.stride(1), b.stride(2), b.stride(0), 0)
+    launch(
+        opa,
+        opb,
+        c,
+        batch1=nb,
+        batch2=1,
+        m=m,
+        n=n,
+        k=k,
+        c_sm=n,
+        c_sn=1,
+        c_s1=m * n,
+        c_s2=0,
+        alpha=alpha,
+    )
+    return c
+
+
+def tile_config(n: int, k: int, dtype: torch.dtype) -> tuple[int, int, int]:
+    """(block_m, block_n, block_k) the library uses for (n, k, dtype)."""
+    code = _lib.load().bio_gemm_tile_config(n, k, _lib.DTYPE_CODE[dtype])
+    return code // 1000000, (code // 1000) % 1000, code % 1000

@@ -1,0 +1,875 @@
+// Batch-invariant GEMM / batched GEMM for sm_100a.
+//
+// bf16 / fp16: persistent, warp-specialised tcgen05 kernel.
+//   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage,
+//               128-byte swizzle, mbarrier ring of STAGES stages.
+//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per stage,
+//               fp32 accumulators in TMEM, double buffered (2 x BN columns).
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, alpha, bias (fp32),
+//               round to the output dtype, store.
+// The tile shape (128 x BN x 64) is a function of (N, K, dtype) only and the
+// K loop always runs k-block 0..K/64-1, MMA-K 16 steps in order, so the bits
+// of output row m depend on row m of A and on B only (never on M, the batch
+// count or the tile a row lands in).  No split-K, no stream-K.
+//
+// fp32: CUDA-core GEMM (128x128x8 tiles, 8x8 outputs per thread); exact fp64
+// products accumulated with DFMA in sequential k order from k = 0, one final
+// rounding to fp32.
+//
+// Reference: matmul_kernel_persistent / bmm_kernel_persistent in
+// batch_invariant_ops/batch_invariant_ops.py:61-229 and their launchers
+// :271-431 (tile table :294-319, input_precision="ieee" :340).
+#include <mutex>
+
+#include "bio_common.cuh"
+
+namespace bio {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+struct TcGemmParams {
+  int m, n, k;
+  int tiles_m, tiles_n, k_blocks;
+  int64_t batch2;
+  int64_t total_tiles;
+  int a_div2, b_div2;
+  int a_bcast1, a_bcast2, b_bcast1, b_bcast2;
+  void* c;
+  int64_t c_sm, c_sn, c_s1, c_s2;
+  const void* bias;
+  int64_t bias_s2;
+  int bias_per_row;
+  float alpha;
+  int c_vec_ok;
+  int* status;
+};
+
+struct TileIdx {
+  int64_t b1, b2;
+  int mb, nb;
+};
+
+// Tile t -> (batch, m-block, n-block).  Grouped raster (8 m-blocks sweep the
+// n-blocks) for L2 reuse; the order only affects which CTA computes a tile,
+// never the arithmetic of the tile.
+__device__ __forceinline__ TileIdx decode_tile(int64_t t, int tiles_m, int tiles_n,
+                                               int64_t batch2) {
+  const int64_t per = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int64_t bi = t / per;
+  const int r = static_cast<int>(t - bi * per);
+  constexpr int kGroupM = 8;
+  const int in_group = kGroupM * tiles_n;
+  const int g = r / in_group;
+  const int first_m = g * kGroupM;
+  const int gsz = min(tiles_m - first_m, kGroupM);
+  const int rr = r - g * in_group;
+  TileIdx ti;
+  ti.mb = first_m + rr % gsz;
+  ti.nb = rr / gsz;
+  ti.b1 = bi / batch2;
+  ti.b2 = bi - ti.b1 * batch2;
+  return ti;
+}
+
+// Wait used only while draining copies at kernel exit: bounded, ignores the
+// abort flag (the copies must land before shared memory is released).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 0; i < kWaitMaxIters; ++i) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+  return false;
+}
+
+template <typename T>
+struct TypeFmt;
+template <>
+struct TypeFmt<__half> {
+  static constexpr uint32_t umma = 0;
+};
+template <>
+struct TypeFmt<__nv_bfloat16> {
+  static constexpr uint32_t umma = 1;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int BN, int STAGES>
+struct TcSmem {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarBytes = (2 * STAGES + 5) * 8 + 16;
+  static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kBarBytes;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcGemmParams p) {
+  using L = TcSmem<BN, STAGES>;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc = idesc_f16(TypeFmt<T>::umma, kBM, BN, A_MN, B_MN);
+  constexpr uint32_t kBoxBytesMN = 64 * kBK * 2;  // one 64(N) x 64(K) box
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * L::kBBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* mma_done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 4);
+    }
+    mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2);
+        const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
+        const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
+        const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * L::kABytes;
+          uint8_t* b_dst = sB + stage * L::kBBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
+          if constexpr (!A_MN) {
+            tma_load_4d(a_dst, &tmA, &full_bar[stage], kb * kBK, ti.mb * kBM, a2, a1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) {
+              tma_load_4d(a_dst + j * kBoxBytesMN, &tmA, &full_bar[stage], ti.mb * kBM + j * 64,
+                          kb * kBK, a2, a1);
+            }
+          }
+          if constexpr (!B_MN) {
+            tma_load_4d(b_dst, &tmB, &full_bar[stage], kb * kBK, ti.nb * BN, b2, b1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_4d(b_dst + j * kBoxBytesMN, &tmB, &full_bar[stage], ti.nb * BN + j * 64,
+                          kb * kBK, b2, b1);
+            }
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the last min(issued, STAGES) loads must land before the CTA
+      // releases its shared memory (normally they already have).
+      const int64_t pending = issued < STAGES ? issued : STAGES;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int64_t i = 0; i < pending; ++i) {
+        if (--s < 0) {
+          s = STAGES - 1;
+          ph ^= 1u;
+        }
+        if (!mbar_wait_drain(&full_bar[s], ph)) raise_status(p.status, BIO_DEV_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? smem_desc_sw128(a_addr + kk * 2048, kBoxBytesMN, 1024)
+                                        : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 2048, kBoxBytesMN, 1024)
+                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Every MMA issued by this thread must retire before TMEM is freed.
+      umma_commit(mma_done_bar);
+      if (!mbar_wait_drain(mma_done_bar, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else {
+    // -------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const T* bias = static_cast<const T*>(p.bias);
+    for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2);
+      const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int m = ti.mb * kBM + q * 32 + lane;
+      T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
+                static_cast<int64_t>(m) * p.c_sm;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) +
+                               (static_cast<uint32_t>(q * 32) << 16),
+                           r);
+        tmem_ld_wait();
+        const int n0 = ti.nb * BN + c0;
+        if (m < p.m && n0 < p.n) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+          if (bias != nullptr) {
+            const T* bb = bias + ti.b2 * p.bias_s2;
+            if (p.bias_per_row) {
+              const float bv = to_f32(bb[m]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += bv;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.n) v[j] += to_f32(bb[n0 + j]);
+            }
+          }
+          if (p.c_vec_ok && n0 + 32 <= p.n) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+              w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+              w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+              w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+              dst[j] = w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fp32 CUDA-core GEMM with fp64 accumulation.
+//
+// Products of two fp32 values are exact in fp64 and the running sum is kept in
+// fp64 (DFMA, sequential k from 0), so the only fp32 rounding is the final
+// store: results sit within ~1 ulp of the exact dot product, far inside the
+// 1e-5 normwise fp32 bar, including the ill-conditioned linspace inputs of
+// the fp32 batch-invariance check where any fp32 accumulation order loses
+// ~5e-4.  Operands are converted to fp64 once when staged into shared memory.
+// ---------------------------------------------------------------------------
+struct F32GemmParams {
+  int64_t m, n, k;
+  int64_t batch2, nbatch;
+  const float* a;
+  int64_t a_sm, a_sk, a_s1, a_s2, a_div2;
+  const float* b;
+  int64_t b_sk, b_sn, b_s1, b_s2, b_div2;
+  float* c;
+  int64_t c_sm, c_sn, c_s1, c_s2;
+  const float* bias;
+  int64_t bias_s2;
+  int bias_per_row;
+  float alpha;
+  int a_kfast, b_nfast;
+};
+
+constexpr int kF32BM = 128, kF32BN = 128, kF32BK = 8;
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const F32GemmParams p) {
+  __shared__ __align__(16) double As[2][kF32BK][kF32BM];
+  __shared__ __align__(16) double Bs[2][kF32BK][kF32BN];
+  const int tid = threadIdx.x;
+  const int tm = tid >> 4, tn = tid & 15;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kF32BM;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kF32BN;
+
+  for (int64_t bi = blockIdx.z; bi < p.nbatch; bi += gridDim.z) {
+    const int64_t b1 = bi / p.batch2, b2 = bi - b1 * p.batch2;
+    const float* A = p.a + b1 * p.a_s1 + (b2 / p.a_div2) * p.a_s2;
+    const float* B = p.b + b1 * p.b_s1 + (b2 / p.b_div2) * p.b_s2;
+    float* C = p.c + b1 * p.c_s1 + b2 * p.c_s2;
+
+    double acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+
+    float ra[4], rb[4];
+    auto load_tile = [&](int64_t k0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int idx = tid + i * 256;
+        int mm, kk;
+        if (p.a_kfast) {
+          kk = idx & 7;
+          mm = idx >> 3;
+        } else {
+          mm = idx & 127;
+          kk = idx >> 7;
+        }
+        const int64_t gm = m0 + mm, gk = k0 + kk;
+        ra[i] = (gm < p.m && gk < p.k) ? A[gm * p.a_sm + gk * p.a_sk] : 0.f;
+        int nn, kb;
+        if (p.b_nfast) {
+          nn = idx & 127;
+          kb = idx >> 7;
+        } else {
+          kb = idx & 7;
+          nn = idx >> 3;
+        }
+        const int64_t gn = n0 + nn, gkb = k0 + kb;
+        rb[i] = (gn < p.n && gkb < p.k) ? B[gkb * p.b_sk + gn * p.b_sn] : 0.f;
+      }
+    };
+    auto store_tile = [&](int buf) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int idx = tid + i * 256;
+        if (p.a_kfast)
+          As[buf][idx & 7][idx >> 3] = static_cast<double>(ra[i]);
+        else
+          As[buf][idx >> 7][idx & 127] = static_cast<double>(ra[i]);
+        if (p.b_nfast)
+          Bs[buf][idx >> 7][idx & 127] = static_cast<double>(rb[i]);
+        else
+          Bs[buf][idx & 7][idx >> 3] = static_cast<double>(rb[i]);
+      }
+    };
+
+    const int64_t k_tiles = (p.k + kF32BK - 1) / kF32BK;
+    load_tile(0);
+    store_tile(0);
+    __syncthreads();
+    for (int64_t kt = 0; kt < k_tiles; ++kt) {
+      const int buf = static_cast<int>(kt & 1);
+      if (kt + 1 < k_tiles) load_tile((kt + 1) * kF32BK);
+#pragma unroll
+      for (int kk = 0; kk < kF32BK; ++kk) {
+        double a[8], b[8];
+        const double2* pa0 = reinterpret_cast<const double2*>(&As[buf][kk][tm * 4]);
+        const double2* pa1 = reinterpret_cast<const double2*>(&As[buf][kk][64 + tm * 4]);
+        const double2* pb0 = reinterpret_cast<const double2*>(&Bs[buf][kk][tn * 4]);
+        const double2* pb1 = reinterpret_cast<const double2*>(&Bs[buf][kk][64 + tn * 4]);
+        double2 t;
+        t = pa0[0]; a[0] = t.x; a[1] = t.y;
+        t = pa0[1]; a[2] = t.x; a[3] = t.y;
+        t = pa1[0]; a[4] = t.x; a[5] = t.y;
+        t = pa1[1]; a[6] = t.x; a[7] = t.y;
+        t = pb0[0]; b[0] = t.x; b[1] = t.y;
+        t = pb0[1]; b[2] = t.x; b[3] = t.y;
+        t = pb1[0]; b[4] = t.x; b[5] = t.y;
+        t = pb1[1]; b[6] = t.x; b[7] = t.y;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+      }
+      if (kt + 1 < k_tiles) store_tile(buf ^ 1);
+      __syncthreads();
+    }
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t gm = m0 + (i < 4 ? tm * 4 + i : 64 + tm * 4 + (i - 4));
+      if (gm >= p.m) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t gn = n0 + (j < 4 ? tn * 4 + j : 64 + tn * 4 + (j - 4));
+        if (gn >= p.n) continue;
+        double v = acc[i][j] * static_cast<double>(p.alpha);
+        if (p.bias != nullptr)
+          v += static_cast<double>(p.bias[b2 * p.bias_s2 + (p.bias_per_row ? gm : gn)]);
+        C[gm * p.c_sm + gn * p.c_sn] = static_cast<float>(v);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// C = alpha * 0 + bias (K == 0): an empty reduction.
+template <typename T>
+__global__ void gemm_fill_kernel(T* c, int64_t m, int64_t n, int64_t nbatch, int64_t batch2,
+                                 int64_t c_sm, int64_t c_sn, int64_t c_s1, int64_t c_s2,
+                                 const T* bias, int64_t bias_s2, int bias_per_row) {
+  const int64_t total = nbatch * m * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t col = i % n;
+    const int64_t row = (i / n) % m;
+    const int64_t bi = i / (n * m);
+    const int64_t b1 = bi / batch2, b2 = bi - b1 * batch2;
+    const float v =
+        bias != nullptr ? to_f32(bias[b2 * bias_s2 + (bias_per_row ? row : col)]) : 0.f;
+    c[b1 * c_s1 + b2 * c_s2 + row * c_sm + col * c_sn] = from_f32<T>(v);
+  }
+}
+
+template <typename T>
+__global__ void pack_rows_kernel(const T* __restrict__ src, int64_t nb2, int64_t rows,
+                                 int64_t cols, int64_t s_b1, int64_t s_b2, int64_t s_row,
+                                 int64_t s_col, T* __restrict__ dst, int64_t cols_pad,
+                                 int64_t total) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t col = i % cols_pad;
+    const int64_t rest = i / cols_pad;
+    const int64_t row = rest % rows;
+    const int64_t b = rest / rows;
+    const int64_t b1 = b / nb2, b2 = b - b1 * nb2;
+    dst[i] = col < cols ? src[b1 * s_b1 + b2 * s_b2 + row * s_row + col * s_col]
+                        : from_f32<T>(0.f);
+  }
+}
+
+}  // namespace bio
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+namespace {
+
+using bio::kBK;
+using bio::kBM;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Operand view for a 4-D tensor map {inner, outer, level2, level1}.
+struct MapDims {
+  uint64_t d[4];
+  uint64_t stride_bytes[3];
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Build the {inner, outer, n2, n1} view of one operand.  Returns false when the
+// strides cannot be expressed to TMA (not multiples of 16 bytes).
+bool operand_dims(uint64_t inner, uint64_t outer, int64_t outer_stride, int64_t batch1,
+                  int64_t s1, int64_t n2_logical, int64_t s2, int64_t div2, MapDims* out,
+                  int* bcast1, int* bcast2) {
+  const int64_t es = 2;
+  if (outer_stride <= 0 || (outer_stride * es) % 16 != 0) return false;
+  out->d[0] = inner;
+  out->d[1] = outer;
+  out->stride_bytes[0] = static_cast<uint64_t>(outer_stride * es);
+  uint64_t prev = out->stride_bytes[0] * outer;
+  prev = (prev + 15) / 16 * 16;
+  // level 2
+  const int64_t n2 = (n2_logical + div2 - 1) / div2;
+  if (s2 == 0 || n2 <= 1) {
+    *bcast2 = (s2 == 0) ? 1 : 0;
+    out->d[2] = 1;
+    out->stride_bytes[1] = prev;
+  } else {
+    if ((s2 * es) % 16 != 0 || s2 < 0) return false;
+    *bcast2 = 0;
+    out->d[2] = static_cast<uint64_t>(n2);
+    out->stride_bytes[1] = static_cast<uint64_t>(s2 * es);
+  }
+  uint64_t prev2 = out->stride_bytes[1] * out->d[2];
+  prev2 = (prev2 + 15) / 16 * 16;
+  if (s1 == 0 || batch1 <= 1) {
+    *bcast1 = (s1 == 0) ? 1 : 0;
+    out->d[3] = 1;
+    out->stride_bytes[2] = prev2;
+  } else {
+    if ((s1 * es) % 16 != 0 || s1 < 0) return false;
+    *bcast1 = 0;
+    out->d[3] = static_cast<uint64_t>(batch1);
+    out->stride_bytes[2] = static_cast<uint64_t>(s1 * es);
+  }
+  for (int i = 0; i < 3; ++i)
+    if (out->stride_bytes[i] >= (1ull << 40)) return false;
+  return true;
+}
+
+int encode_map(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md, uint32_t box0,
+               uint32_t box1) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return BIO_ERR_DRIVER;
+  const CUtensorMapDataType dt =
+      dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[4] = {md.d[0], md.d[1], md.d[2], md.d[3]};
+  cuuint64_t strides[3] = {md.stride_bytes[0], md.stride_bytes[1], md.stride_bytes[2]};
+  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
+}
+
+// Tile N chosen from (n, k, dtype) only.  Wide N tiles for wide outputs (more
+// reuse of A per byte of B), narrow ones for narrow outputs so that even a
+// single row (M = 1) spreads the weight stream over many SMs.
+int pick_bn(int64_t n, int64_t /*k*/, int32_t /*dtype*/) {
+  if (n >= 32768) return 256;
+  if (n >= 8192) return 128;
+  return 64;
+}
+
+template <int BN>
+constexpr int stages_for() {
+  return BN == 64 ? 8 : (BN == 128 ? 6 : 4);
+}
+
+std::mutex g_attr_mu;
+
+template <int BN, bool A_MN, bool B_MN, typename T>
+int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
+  constexpr int STAGES = stages_for<BN>();
+  using L = bio::TcSmem<BN, STAGES>;
+  auto kern = bio::gemm_tc_kernel<BN, STAGES, A_MN, B_MN, T>;
+
+  static bool attr_done[bio_host::kMaxDevices] = {false};
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (!attr_done[a->device]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+          cudaSuccess)
+        return BIO_ERR_LAUNCH;
+      attr_done[a->device] = true;
+    }
+  }
+
+  const int64_t batch = a->batch1 * a->batch2;
+  MapDims ma, mb;
+  int a_b1 = 0, a_b2 = 0, b_b1 = 0, b_b2 = 0;
+  if (!A_MN) {
+    if (!operand_dims(static_cast<uint64_t>(a->k), static_cast<uint64_t>(a->m), a->a_sm,
+                      a->batch1, a->a_s1, a->batch2, a->a_s2, a->a_div2, &ma, &a_b1, &a_b2))
+      return BIO_ERR_ALIGN;
+  } else {
+    if (!operand_dims(static_cast<uint64_t>(a->m), static_cast<uint64_t>(a->k), a->a_sk,
+                      a->batch1, a->a_s1, a->batch2, a->a_s2, a->a_div2, &ma, &a_b1, &a_b2))
+      return BIO_ERR_ALIGN;
+  }
+  if (!B_MN) {
+    if (!operand_dims(static_cast<uint64_t>(a->k), static_cast<uint64_t>(a->n), a->b_sn,
+                      a->batch1, a->b_s1, a->batch2, a->b_s2, a->b_div2, &mb, &b_b1, &b_b2))
+      return BIO_ERR_ALIGN;
+  } else {
+    if (!operand_dims(static_cast<uint64_t>(a->n), static_cast<uint64_t>(a->k), a->b_sk,
+                      a->batch1, a->b_s1, a->batch2, a->b_s2, a->b_div2, &mb, &b_b1, &b_b2))
+      return BIO_ERR_ALIGN;
+  }
+  CUtensorMap tmA, tmB;
+  int st = A_MN ? encode_map(&tmA, a->dtype, a->a, ma, 64, kBK)
+                : encode_map(&tmA, a->dtype, a->a, ma, kBK, kBM);
+  if (st != BIO_OK) return st;
+  st = B_MN ? encode_map(&tmB, a->dtype, a->b, mb, 64, kBK)
+            : encode_map(&tmB, a->dtype, a->b, mb, kBK, BN);
+  if (st != BIO_OK) return st;
+
+  bio::TcGemmParams p;
+  p.m = static_cast<int>(a->m);
+  p.n = static_cast<int>(a->n);
+  p.k = static_cast<int>(a->k);
+  p.tiles_m = static_cast<int>((a->m + kBM - 1) / kBM);
+  p.tiles_n = static_cast<int>((a->n + BN - 1) / BN);
+  p.k_blocks = static_cast<int>((a->k + kBK - 1) / kBK);
+  p.batch2 = a->batch2;
+  p.total_tiles = batch * p.tiles_m * p.tiles_n;
+  p.a_div2 = static_cast<int>(a->a_div2);
+  p.b_div2 = static_cast<int>(a->b_div2);
+  p.a_bcast1 = a_b1;
+  p.a_bcast2 = a_b2;
+  p.b_bcast1 = b_b1;
+  p.b_bcast2 = b_b2;
+  p.c = a->c;
+  p.c_sm = a->c_sm;
+  p.c_sn = a->c_sn;
+  p.c_s1 = a->c_s1;
+  p.c_s2 = a->c_s2;
+  p.bias = a->bias;
+  p.bias_s2 = a->bias_s2;
+  p.bias_per_row = (a->flags & BIO_GEMM_BIAS_PER_ROW) ? 1 : 0;
+  p.alpha = a->alpha;
+  p.c_vec_ok = (a->c_sn == 1 && aligned16(a->c) && (a->c_sm * 2) % 16 == 0 &&
+                (a->c_s1 * 2) % 16 == 0 && (a->c_s2 * 2) % 16 == 0)
+                   ? 1
+                   : 0;
+  p.status = bio_host::status_word(a->device);
+
+  const int sms = bio_host::sm_count(a->device);
+  if (sms <= 0) return BIO_ERR_LAUNCH;
+  const int64_t grid = p.total_tiles < sms ? p.total_tiles : sms;
+  kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, L::kTotal, stream>>>(tmA, tmB, p);
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+template <bool A_MN, bool B_MN, typename T>
+int dispatch_bn(const bio_gemm_args* a, cudaStream_t stream) {
+  switch (pick_bn(a->n, a->k, a->dtype)) {
+    case 64: return launch_tc<64, A_MN, B_MN, T>(a, stream);
+    case 128: return launch_tc<128, A_MN, B_MN, T>(a, stream);
+    default: return launch_tc<256, A_MN, B_MN, T>(a, stream);
+  }
+}
+
+template <typename T>
+int dispatch_tc(const bio_gemm_args* a, cudaStream_t stream, bool a_mn, bool b_mn) {
+  if (a_mn) {
+    return b_mn ? dispatch_bn<true, true, T>(a, stream) : dispatch_bn<true, false, T>(a, stream);
+  }
+  return b_mn ? dispatch_bn<false, true, T>(a, stream) : dispatch_bn<false, false, T>(a, stream);
+}
+
+int launch_f32(const bio_gemm_args* a, cudaStream_t stream) {
+  bio::F32GemmParams p;
+  p.m = a->m;
+  p.n = a->n;
+  p.k = a->k;
+  p.batch2 = a->batch2;
+  p.nbatch = a->batch1 * a->batch2;
+  p.a = static_cast<const float*>(a->a);
+  p.a_sm = a->a_sm;
+  p.a_sk = a->a_sk;
+  p.a_s1 = a->a_s1;
+  p.a_s2 = a->a_s2;
+  p.a_div2 = a->a_div2;
+  p.b = static_cast<const float*>(a->b);
+  p.b_sk = a->b_sk;
+  p.b_sn = a->b_sn;
+  p.b_s1 = a->b_s1;
+  p.b_s2 = a->b_s2;
+  p.b_div2 = a->b_div2;
+  p.c = static_cast<float*>(a->c);
+  p.c_sm = a->c_sm;
+  p.c_sn = a->c_sn;
+  p.c_s1 = a->c_s1;
+  p.c_s2 = a->c_s2;
+  p.bias = static_cast<const float*>(a->bias);
+  p.bias_s2 = a->bias_s2;
+  p.bias_per_row = (a->flags & BIO_GEMM_BIAS_PER_ROW) ? 1 : 0;
+  p.alpha = a->alpha;
+  p.a_kfast = (a->a_sk == 1) ? 1 : 0;
+  p.b_nfast = (a->b_sn == 1) ? 1 : 0;
+  const int64_t gx = (a->n + bio::kF32BN - 1) / bio::kF32BN;
+  const int64_t gy = (a->m + bio::kF32BM - 1) / bio::kF32BM;
+  if (gx > 2147483647 || gy > 65535) return BIO_ERR_SHAPE;
+  const int64_t nb = p.nbatch;
+  const unsigned gz = static_cast<unsigned>(nb < 65535 ? nb : 65535);
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), gz);
+  bio::gemm_f32_kernel<<<grid, 256, 0, stream>>>(p);
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+template <typename T>
+int launch_fill(const bio_gemm_args* a, cudaStream_t stream) {
+  const int64_t total = a->batch1 * a->batch2 * a->m * a->n;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 65536) blocks = 65536;
+  bio::gemm_fill_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<T*>(a->c), a->m, a->n, a->batch1 * a->batch2, a->batch2, a->c_sm, a->c_sn,
+      a->c_s1, a->c_s2, static_cast<const T*>(a->bias), a->bias_s2,
+      (a->flags & BIO_GEMM_BIAS_PER_ROW) ? 1 : 0);
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" {
+
+int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype) {
+  if (dtype == BIO_F32) return bio::kF32BM * 1000000 + bio::kF32BN * 1000 + bio::kF32BK;
+  return kBM * 1000000 + pick_bn(n, k, dtype) * 1000 + kBK;
+}
+
+int bio_gemm(const bio_gemm_args* a, void* stream_v) {
+  if (a == nullptr) return BIO_ERR_ARG;
+  if ((a->flags & ~BIO_GEMM_BIAS_PER_ROW) != 0) return BIO_ERR_ARG;
+  if (a->m < 0 || a->n < 0 || a->k < 0 || a->batch1 < 0 || a->batch2 < 1) return BIO_ERR_SHAPE;
+  if (a->a_div2 < 1 || a->b_div2 < 1) return BIO_ERR_ARG;
+  if (a->dtype != BIO_F32 && a->dtype != BIO_F16 && a->dtype != BIO_BF16) return BIO_ERR_DTYPE;
+  const int64_t batch = a->batch1 * a->batch2;
+  if (batch == 0 || a->m == 0 || a->n == 0) return BIO_OK;
+  if (a->c == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(a->device);
+  if (st != BIO_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+
+  if (a->k == 0) {
+    switch (a->dtype) {
+      case BIO_F32: return launch_fill<float>(a, stream);
+      case BIO_F16: return launch_fill<__half>(a, stream);
+      default: return launch_fill<__nv_bfloat16>(a, stream);
+    }
+  }
+  if (a->a == nullptr || a->b == nullptr) return BIO_ERR_ARG;
+  if (a->dtype == BIO_F32) return launch_f32(a, stream);
+
+  // Tensor-core path: TMA needs 16-byte aligned bases and strides, K-contiguous A
+  // and K- or N-contiguous B; int32 tile coordinates.
+  if (a->m > 2147483647 || a->n > 2147483647 || a->k > 2147483647) return BIO_ERR_SHAPE;
+  if (a->batch1 > 2147483647 || a->batch2 > 2147483647) return BIO_ERR_SHAPE;
+  if (!aligned16(a->a) || !aligned16(a->b)) return BIO_ERR_ALIGN;
+  bool a_mn;
+  if (a->a_sk == 1) {
+    a_mn = false;
+  } else if (a->a_sm == 1) {
+    a_mn = true;
+  } else {
+    return BIO_ERR_STRIDE;
+  }
+  bool b_mn;
+  if (a->b_sk == 1) {
+    b_mn = false;
+  } else if (a->b_sn == 1) {
+    b_mn = true;
+  } else {
+    return BIO_ERR_STRIDE;
+  }
+  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, stream, a_mn, b_mn);
+  return dispatch_tc<__half>(a, stream, a_mn, b_mn);
+}
+
+int bio_pack_rows(int32_t dtype, const void* src, int64_t nb1, int64_t nb2, int64_t rows,
+                  int64_t cols, int64_t s_b1, int64_t s_b2, int64_t s_row, int64_t s_col,
+                  void* dst, int64_t cols_pad, int32_t device, void* stream_v) {
+  if (nb1 < 0 || nb2 < 0 || rows < 0 || cols < 0 || cols_pad < cols) return BIO_ERR_SHAPE;
+  const int64_t total = nb1 * nb2 * rows * cols_pad;
+  if (total == 0) return BIO_OK;
+  if (src == nullptr || dst == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 65536) blocks = 65536;
+  const unsigned g = static_cast<unsigned>(blocks);
+  switch (dtype) {
+    case BIO_F32:
+      bio::pack_rows_kernel<float><<<g, 256, 0, stream>>>(
+          static_cast<const float*>(src), nb2, rows, cols, s_b1, s_b2, s_row, s_col,
+          static_cast<float*>(dst), cols_pad, total);
+      break;
+    case BIO_F16:
+      bio::pack_rows_kernel<__half><<<g, 256, 0, stream>>>(
+          static_cast<const __half*>(src), nb2, rows, cols, s_b1, s_b2, s_row, s_col,
+          static_cast<__half*>(dst), cols_pad, total);
+      break;
+    case BIO_BF16:
+      bio::pack_rows_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(src), nb2, rows, cols, s_b1, s_b2, s_row, s_col,
+          static_cast<__nv_bfloat16*>(dst), cols_pad, total);
+      break;
+    default: return BIO_ERR_DTYPE;
+  }
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+}  // extern "C"

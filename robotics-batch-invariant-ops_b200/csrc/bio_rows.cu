@@ -1,0 +1,299 @@
+// Batch-invariant row kernels: softmax, log-softmax, mean, L2 norm.
+//
+// The input is a contiguous [outer][n][inner] view reduced over n.
+//
+// Row mode (inner == 1): a fixed team of threads owns one row.  The team size
+// is a function of n only (32, 256 or 1024 threads).  Element i belongs to the
+// 8-element group i/8, group g to thread g % team, each thread folds its groups
+// in increasing g (elements of a group in order), then a fixed xor-shuffle tree
+// combines the warp and, for multi-warp teams, warp 0 combines the per-warp
+// partials in warp order.  16-byte vector loads are used when a group is
+// aligned; that changes the load instruction, never the order of the sums.
+//
+// Column mode (inner > 1): one thread owns one output column and folds the n
+// elements in increasing order (loads coalesced across columns).
+//
+// Either way the reduction tree of an output depends on n alone, never on the
+// number of rows/columns, so every output is batch invariant.  All arithmetic
+// is fp32; the result is rounded once to the output dtype.
+//
+// Reference: _softmax_kernel / softmax (batch_invariant_ops.py:1075-1145),
+// _log_softmax_kernel / log_softmax (:975-1071), mean_kernel / mean_dim
+// (:1348-1482), _vector_norm_kernel / linalg_vector_norm_batch_invariant
+// (:1486-1597).
+#include "bio_common.cuh"
+
+namespace bio {
+
+enum RowOp : int { kSoftmax = 0, kLogSoftmax = 1, kMean = 2, kL2Norm = 3 };
+
+template <typename T>
+__device__ __forceinline__ void load_group(const T* __restrict__ row, int64_t g, int64_t n,
+                                           float (&v)[8], float fill) {
+  const int64_t base = g * 8;
+  const T* p = row + base;
+  if (base + 8 <= n && (reinterpret_cast<uintptr_t>(p) % 16) == 0 && sizeof(T) == 2) {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = to_f32(e[j]);
+  } else if (base + 8 <= n && (reinterpret_cast<uintptr_t>(p) % 16) == 0 && sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (base + j < n) ? to_f32(p[j]) : fill;
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return __shfl_sync(0xffffffffu, v, 0);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return __shfl_sync(0xffffffffu, v, 0);
+}
+
+// Team-wide reduction with a fixed tree.  `scratch` holds TEAM/32 floats per
+// team; all threads of the team receive the result of the tree.
+template <int TEAM, bool IS_MAX>
+__device__ __forceinline__ float team_reduce(float v, float* scratch) {
+  v = IS_MAX ? warp_max(v) : warp_sum(v);
+  if constexpr (TEAM == 32) {
+    return v;
+  } else {
+    constexpr int W = TEAM / 32;
+    const int t = threadIdx.x % TEAM;
+    const int w = t >> 5, lane = t & 31;
+    __syncthreads();
+    if (lane == 0) scratch[w] = v;
+    __syncthreads();
+    float r;
+    if (w == 0) {
+      float x = lane < W ? scratch[lane] : (IS_MAX ? -INFINITY : 0.f);
+      r = IS_MAX ? warp_max(x) : warp_sum(x);
+      if (lane == 0) scratch[W] = r;
+    }
+    __syncthreads();
+    r = scratch[W];
+    return r;
+  }
+}
+
+template <typename TI, typename TO, int OP, int TEAM>
+__global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
+    row_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t rows, int64_t n) {
+  constexpr int kTeamsPerBlock = TEAM >= 256 ? 1 : 256 / TEAM;
+  __shared__ float scratch[kTeamsPerBlock][TEAM / 32 + 1];
+  const int team = threadIdx.x / TEAM;
+  const int t = threadIdx.x % TEAM;
+  const int64_t groups = (n + 7) / 8;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTeamsPerBlock + team; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * kTeamsPerBlock) {
+    const TI* row = x + r * n;
+    if constexpr (OP == kMean || OP == kL2Norm) {
+      float acc = 0.f;
+      for (int64_t g = t; g < groups; g += TEAM) {
+        float v[8];
+        load_group(row, g, n, v, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc += (OP == kL2Norm) ? v[j] * v[j] : v[j];
+      }
+      const float s = team_reduce<TEAM, false>(acc, scratch[team]);
+      if (t == 0) {
+        const float out = (OP == kMean) ? s / static_cast<float>(n) : sqrtf(s);
+        y[r] = from_f32<TO>(out);
+      }
+    } else {
+      float mx = -INFINITY;
+      for (int64_t g = t; g < groups; g += TEAM) {
+        float v[8];
+        load_group(row, g, n, v, -INFINITY);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[j]);
+      }
+      mx = team_reduce<TEAM, true>(mx, scratch[team]);
+      float den = 0.f;
+      for (int64_t g = t; g < groups; g += TEAM) {
+        float v[8];
+        load_group(row, g, n, v, -INFINITY);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (g * 8 + j < n) {
+            if constexpr (OP == kSoftmax)
+              den += (mx == -INFINITY) ? 0.f : expf(v[j] - mx);
+            else
+              den += expf(v[j] - mx);
+          }
+        }
+      }
+      den = team_reduce<TEAM, false>(den, scratch[team]);
+      TO* out = y + r * n;
+      if constexpr (OP == kSoftmax) {
+        const float inv_ok = den != 0.f;
+        for (int64_t i = t; i < n; i += TEAM) {
+          const float v = to_f32(row[i]);
+          const float e = (mx == -INFINITY) ? 0.f : expf(v - mx);
+          out[i] = from_f32<TO>(inv_ok ? e / den : 0.f);
+        }
+      } else {
+        const float lse = logf(den);
+        for (int64_t i = t; i < n; i += TEAM) {
+          const float v = to_f32(row[i]);
+          out[i] = from_f32<TO>(v - mx - lse);
+        }
+      }
+    }
+  }
+}
+
+// Column mode: one thread per (outer, inner) column, sequential over n.
+template <typename TI, typename TO, int OP>
+__global__ void __launch_bounds__(256)
+    col_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t outer, int64_t n,
+               int64_t inner) {
+  const int64_t cols = outer * inner;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < cols;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = c / inner, i = c - o * inner;
+    const TI* base = x + o * n * inner + i;
+    if constexpr (OP == kMean || OP == kL2Norm) {
+      float acc = 0.f;
+      for (int64_t j = 0; j < n; ++j) {
+        const float v = to_f32(base[j * inner]);
+        acc += (OP == kL2Norm) ? v * v : v;
+      }
+      y[c] = from_f32<TO>((OP == kMean) ? acc / static_cast<float>(n) : sqrtf(acc));
+    } else {
+      float mx = -INFINITY;
+      for (int64_t j = 0; j < n; ++j) mx = fmaxf(mx, to_f32(base[j * inner]));
+      float den = 0.f;
+      for (int64_t j = 0; j < n; ++j) {
+        const float v = to_f32(base[j * inner]);
+        if constexpr (OP == kSoftmax)
+          den += (mx == -INFINITY) ? 0.f : expf(v - mx);
+        else
+          den += expf(v - mx);
+      }
+      TO* out = y + o * n * inner + i;
+      if constexpr (OP == kSoftmax) {
+        for (int64_t j = 0; j < n; ++j) {
+          const float v = to_f32(base[j * inner]);
+          const float e = (mx == -INFINITY) ? 0.f : expf(v - mx);
+          out[j * inner] = from_f32<TO>(den != 0.f ? e / den : 0.f);
+        }
+      } else {
+        const float lse = logf(den);
+        for (int64_t j = 0; j < n; ++j) out[j * inner] = from_f32<TO>(to_f32(base[j * inner]) - mx - lse);
+      }
+    }
+  }
+}
+
+}  // namespace bio
+
+namespace {
+
+// Team size of row mode: a function of the row length only.
+int team_for(int64_t n) {
+  if (n <= 2048) return 32;
+  if (n <= 32768) return 256;
+  return 1024;
+}
+
+template <typename TI, typename TO, int OP>
+int launch_rows(const void* x, void* y, int64_t outer, int64_t n, int64_t inner,
+                cudaStream_t stream, int sms) {
+  const TI* xi = static_cast<const TI*>(x);
+  TO* yo = static_cast<TO*>(y);
+  if (inner == 1) {
+    const int team = team_for(n);
+    const int64_t per_block = team >= 256 ? 1 : 256 / team;
+    int64_t blocks = (outer + per_block - 1) / per_block;
+    const int64_t cap = static_cast<int64_t>(sms) * 32;
+    if (blocks > cap) blocks = cap;
+    const unsigned g = static_cast<unsigned>(blocks);
+    switch (team) {
+      case 32: bio::row_kernel<TI, TO, OP, 32><<<g, 256, 0, stream>>>(xi, yo, outer, n); break;
+      case 256: bio::row_kernel<TI, TO, OP, 256><<<g, 256, 0, stream>>>(xi, yo, outer, n); break;
+      default: bio::row_kernel<TI, TO, OP, 1024><<<g, 1024, 0, stream>>>(xi, yo, outer, n); break;
+    }
+  } else {
+    const int64_t cols = outer * inner;
+    int64_t blocks = (cols + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sms) * 64;
+    if (blocks > cap) blocks = cap;
+    bio::col_kernel<TI, TO, OP><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(xi, yo, outer,
+                                                                                  n, inner);
+  }
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+template <int OP, typename TI>
+int dispatch_out(int dtype_out, const void* x, void* y, int64_t outer, int64_t n, int64_t inner,
+                 cudaStream_t s, int sms) {
+  switch (dtype_out) {
+    case BIO_F32: return launch_rows<TI, float, OP>(x, y, outer, n, inner, s, sms);
+    case BIO_F16: return launch_rows<TI, __half, OP>(x, y, outer, n, inner, s, sms);
+    case BIO_BF16: return launch_rows<TI, __nv_bfloat16, OP>(x, y, outer, n, inner, s, sms);
+    default: return BIO_ERR_DTYPE;
+  }
+}
+
+template <int OP>
+int dispatch(int dtype_in, int dtype_out, const void* x, void* y, int64_t outer, int64_t n,
+             int64_t inner, cudaStream_t s, int sms) {
+  switch (dtype_in) {
+    case BIO_F32: return dispatch_out<OP, float>(dtype_out, x, y, outer, n, inner, s, sms);
+    case BIO_F16: return dispatch_out<OP, __half>(dtype_out, x, y, outer, n, inner, s, sms);
+    case BIO_BF16: return dispatch_out<OP, __nv_bfloat16>(dtype_out, x, y, outer, n, inner, s, sms);
+    default: return BIO_ERR_DTYPE;
+  }
+}
+
+int check_common(const void* x, void* y, int64_t outer, int64_t n, int64_t inner, int device) {
+  if (outer < 0 || n < 0 || inner < 0) return BIO_ERR_SHAPE;
+  if (outer * inner == 0) return BIO_OK;
+  if (x == nullptr || y == nullptr) return BIO_ERR_ARG;
+  return bio_host::ensure_device(device);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bio_softmax(int32_t dtype_in, int32_t dtype_out, const void* x, void* y, int64_t outer,
+                int64_t n, int64_t inner, int32_t log_softmax, int32_t device, void* stream) {
+  int st = check_common(x, y, outer, n, inner, device);
+  if (st != BIO_OK || outer * inner == 0 || n == 0) return st;
+  const int sms = bio_host::sm_count(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (log_softmax) {
+    if (dtype_out != dtype_in) return BIO_ERR_DTYPE;
+    return dispatch<bio::kLogSoftmax>(dtype_in, dtype_out, x, y, outer, n, inner, s, sms);
+  }
+  return dispatch<bio::kSoftmax>(dtype_in, dtype_out, x, y, outer, n, inner, s, sms);
+}
+
+int bio_reduce(int32_t kind, int32_t dtype_in, int32_t dtype_out, const void* x, void* y,
+               int64_t outer, int64_t n, int64_t inner, int32_t device, void* stream) {
+  int st = check_common(x, y, outer, n, inner, device);
+  if (st != BIO_OK || outer * inner == 0) return st;
+  const int sms = bio_host::sm_count(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (kind) {
+    case BIO_REDUCE_MEAN:
+      return dispatch<bio::kMean>(dtype_in, dtype_out, x, y, outer, n, inner, s, sms);
+    case BIO_REDUCE_L2NORM:
+      return dispatch<bio::kL2Norm>(dtype_in, dtype_out, x, y, outer, n, inner, s, sms);
+    default: return BIO_ERR_ARG;
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,193 @@
+"""GPU parity and batch-invariance tests of the GEMM family (mm, addmm, linear, bmm).
+
+Mirrors test_batch_invariance.py:42-172 of the reference suite and adds the
+BASELINE sweep geometry (K = 4096, N in {4096, 11008}, M from 1 to 2048)
+checked bitwise row-by-row and against the fp64 oracle.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from batch_invariant_ops import bmm_persistent, linear_batch_invariant, matmul_persistent
+from conftest import DTYPES, TOLERANCES, assert_first_sample_equal
+from oracle import bio_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _randn(*shape, dtype, gen, scale=1.0):
+    return (torch.randn(*shape, device="cuda", generator=gen) * scale).to(dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch_size", (2, 3, 5, 17))
+def test_mm_is_batch_invariant(dtype, batch_size):
+    gen = torch.Generator(device="cuda").manual_seed(1000 + batch_size)
+    inputs = _randn(batch_size, 257, dtype=dtype, gen=gen)
+    weight = _randn(257, 129, dtype=dtype, gen=gen)
+    assert_first_sample_equal(matmul_persistent(inputs[:1], weight), matmul_persistent(inputs, weight))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_mm_matches_oracle(dtype):
+    gen = torch.Generator(device="cuda").manual_seed(2000)
+    left = _randn(37, 257, dtype=dtype, gen=gen)
+    right = _randn(257, 91, dtype=dtype, gen=gen)
+    out = matmul_persistent(left, right)
+    torch.testing.assert_close(out.double().cpu(), O.mm(left, right), **TOLERANCES[dtype])
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch_size", (2, 5, 17))
+def test_rank3_linear_is_batch_invariant(dtype, batch_size):
+    gen = torch.Generator(device="cuda").manual_seed(2500 + batch_size)
+    inputs = _randn(batch_size, 37, 257, dtype=dtype, gen=gen)
+    weight = _randn(91, 257, dtype=dtype, gen=gen)
+    bias = _randn(91, dtype=dtype, gen=gen)
+    assert_first_sample_equal(
+        linear_batch_invariant(inputs[:1], weight, bias), linear_batch_invariant(inputs, weight, bias)
+    )
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_linear_matches_torch_and_oracle(dtype):
+    gen = torch.Generator(device="cuda").manual_seed(2700)
+    inputs = _randn(3, 37, 257, dtype=dtype, gen=gen)
+    weight = _randn(91, 257, dtype=dtype, gen=gen)
+    bias = _randn(91, dtype=dtype, gen=gen)
+    out = linear_batch_invariant(inputs, weight, bias)
+    tol = {"rtol": 2e-2, "atol": 1.5e-1} if dtype == torch.bfloat16 else TOLERANCES[dtype]
+    torch.testing.assert_close(out, F.linear(inputs, weight, bias), **tol)
+    torch.testing.assert_close(out.double().cpu(), O.linear(inputs, weight, bias), **tol)
+
+
+def test_projector_shape_is_batch_invariant():
+    gen = torch.Generator(device="cuda").manual_seed(2750)
+    inputs = _randn(2, 256, 1024, dtype=torch.bfloat16, gen=gen)
+    weight = _randn(4096, 1024, dtype=torch.bfloat16, gen=gen)
+    bias = _randn(4096, dtype=torch.bfloat16, gen=gen)
+    assert_first_sample_equal(
+        linear_batch_invariant(inputs[:1], weight, bias), linear_batch_invariant(inputs, weight, bias)
+    )
+
+
+def test_fp32_fov_projection_is_batch_invariant():
+    gen = torch.Generator(device="cuda").manual_seed(2775)
+    inputs = _randn(2, 2304, dtype=torch.float32, gen=gen)
+    weight = _randn(2304, 2304, dtype=torch.float32, gen=gen)
+    bias = _randn(2304, dtype=torch.float32, gen=gen)
+    assert_first_sample_equal(
+        linear_batch_invariant(inputs[:1], weight, bias), linear_batch_invariant(inputs, weight, bias)
+    )
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch_size", (2, 3, 5, 17))
+def test_bmm_is_batch_invariant(dtype, batch_size):
+    gen = torch.Generator(device="cuda").manual_seed(3000 + batch_size)
+    left = _randn(batch_size, 33, 65, dtype=dtype, gen=gen)
+    right = _randn(batch_size, 65, 47, dtype=dtype, gen=gen)
+    assert_first_sample_equal(bmm_persistent(left[:1], right[:1]), bmm_persistent(left, right))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_bmm_matches_oracle_for_noncontiguous_attention_inputs(dtype):
+    gen = torch.Generator(device="cuda").manual_seed(4000)
+    query = _randn(4, 8, 33, 65, dtype=dtype, gen=gen).reshape(-1, 33, 65)
+    key = _randn(4, 8, 47, 65, dtype=dtype, gen=gen).reshape(-1, 47, 65).transpose(1, 2)
+    out = bmm_persistent(query, key)
+    torch.testing.assert_close(out, torch.bmm(query, key), **TOLERANCES[dtype])
+    torch.testing.assert_close(out.double().cpu(), O.bmm(query, key), **TOLERANCES[dtype])
+
+
+def test_bmm_supports_more_than_cuda_grid_y_limit():
+    gen = torch.Generator(device="cuda").manual_seed(4500)
+    left = _randn(70_000, 1, 4, dtype=torch.bfloat16, gen=gen)
+    right = _randn(70_000, 4, 1, dtype=torch.bfloat16, gen=gen)
+    batched = bmm_persistent(left, right)
+    assert_first_sample_equal(bmm_persistent(left[:1], right[:1]), batched)
+    torch.testing.assert_close(batched.double().cpu(), O.bmm(left, right), **TOLERANCES[torch.bfloat16])
+
+
+def test_bmm_broadcast_weight_stride_zero():
+    gen = torch.Generator(device="cuda").manual_seed(4600)
+    x = _randn(6, 40, 64, dtype=torch.bfloat16, gen=gen)
+    w = _randn(64, 96, dtype=torch.bfloat16, gen=gen).unsqueeze(0).expand(6, -1, -1)
+    out = bmm_persistent(x, w)
+    torch.testing.assert_close(out.double().cpu(), O.bmm(x, w), **TOLERANCES[torch.bfloat16])
+    assert_first_sample_equal(bmm_persistent(x[:1], w[:1]), out)
+
+
+@pytest.mark.parametrize(
+    "name", ["mm_f32", "addmm_f32", "linear_f32", "bmm_f32", "mm_f16", "addmm_f16", "linear_f16", "bmm_f16"]
+)
+def test_gemm_matches_reference_golden(name):
+    case = torch.load(GOLDEN / f"{name}.pt", weights_only=False)
+    x = {k: v.cuda() for k, v in case["inputs"].items()}
+    if case["op"] == "mm":
+        out = matmul_persistent(x["a"], x["b"], x.get("bias"))
+    elif case["op"] == "linear":
+        out = linear_batch_invariant(x["x"], x["weight"], x["bias"])
+    else:
+        out = bmm_persistent(x["a"], x["b"])
+    golden = case["output"]
+    tol = dict(TOLERANCES[golden.dtype])
+    if golden.dtype == torch.float16:
+        tol = {"rtol": 2e-3, "atol": 2e-2}
+    torch.testing.assert_close(out.cpu(), golden, **tol)
+
+
+# ---- BASELINE config 2 geometry: bf16 linear sweep, bitwise per row ------
+@pytest.mark.parametrize("n", (4096, 11008))
+@pytest.mark.parametrize("layout", ("linear", "addmm"))
+def test_sweep_rows_are_bitwise_invariant(n, layout):
+    gen = torch.Generator(device="cuda").manual_seed(n)
+    k = 4096
+    x = torch.randn(2048, k, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda", generator=gen) / 64).to(torch.bfloat16)
+    bias = (torch.randn(n, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    if layout == "linear":
+        run = lambda rows: linear_batch_invariant(rows, w, bias)  # noqa: E731
+    else:
+        wt = w.t().contiguous()  # [K, N] row-major: N-contiguous B operand
+        run = lambda rows: matmul_persistent(rows, wt, bias)  # noqa: E731
+    full = run(x)
+    for m in (1, 8, 32, 127, 128, 129, 512):
+        part = run(x[:m])
+        assert torch.equal(part, full[:m]), f"M={m} rows differ from the M=2048 run"
+    # an unrelated companion batch: the first row must not move
+    other = torch.cat([x[:1], torch.randn(300, k, device="cuda", generator=gen).to(torch.bfloat16)])
+    assert torch.equal(run(other)[:1], full[:1])
+    rows = [0, 1, 127, 128, 2047]
+    ref = O.linear(x[rows], w, bias)
+    torch.testing.assert_close(full[rows].double().cpu(), ref, rtol=1e-2, atol=1e-2)
+
+
+def test_fp32_linspace_config1_is_batch_invariant():
+    """BASELINE config 1 (README.md:63-76 of the reference): fp32 linspace mm."""
+    b, d = 2048, 4096
+    a = torch.linspace(-100, 100, b * d, device="cuda").reshape(b, d)
+    w = torch.linspace(-100, 100, d * d, device="cuda").reshape(d, d)
+    full = matmul_persistent(a, w)
+    assert torch.equal(matmul_persistent(a[:1], w), full[:1])
+    rows = [0, 1, 1000, 2047]
+    ref = O.mm(a[rows], w)
+    err = (full[rows].double().cpu() - ref).norm() / ref.norm()
+    assert err < 1e-5, err
+
+
+def test_odd_shapes_and_empty():
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    for m, k, n in ((1, 1, 1), (3, 5, 7), (130, 65, 257), (5, 0, 9)):
+        a = _randn(m, k, dtype=torch.bfloat16, gen=gen)
+        b = _randn(k, n, dtype=torch.bfloat16, gen=gen)
+        out = matmul_persistent(a, b)
+        torch.testing.assert_close(out.double().cpu(), O.mm(a, b), rtol=2e-2, atol=2e-2)
+    empty = matmul_persistent(torch.empty(0, 8, device="cuda"), torch.randn(8, 3, device="cuda"))
+    assert empty.shape == (0, 3)
