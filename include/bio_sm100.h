@@ -152,6 +152,121 @@ BIO_API int bio_reduce(int32_t kind, int32_t dtype_in, int32_t dtype_out, const 
                        void* y, int64_t outer, int64_t n, int64_t inner, int32_t device,
                        void* stream);
 
+/* ---- convolution lowering -------------------------------------------------
+ * Geometry of an N-d convolution, N <= 3, in NC[D][H]W layout; unused
+ * leading spatial dims have in = kernel = stride = dilation = out = 1 and
+ * padding 0.  For transposed convolution `in` is the input spatial size and
+ * `kernel` equals the stride (non-overlapping). */
+typedef struct bio_conv_geom {
+  int64_t batch, channels, groups;
+  int64_t in[3], kernel[3], stride[3], padding[3], dilation[3], out[3];
+} bio_conv_geom;
+
+/* Gather receptive fields of CONTIGUOUS x [B][C][in...] into patches
+ * [B][G][L][kpad] (L = prod(out), K = C/G * prod(kernel) <= kpad, zero tail
+ * and zero padding), K index = (c, kd, kh, kw) row-major like the weight.
+ * The caller then runs one bio_gemm per (sample, group).  Replaces the
+ * F.unfold / as_strided im2col of conv1d/2d/3d_batch_invariant
+ * (batch_invariant_ops.py:566-595, 640-667, 731-760). */
+BIO_API int bio_im2col(int32_t dtype, const void* x, const bio_conv_geom* geom, void* patches,
+                       int64_t kpad, int32_t device, void* stream);
+
+/* Depthwise 1-D convolution (groups == C == O, one tap row per channel):
+ * y[b,c,l] = sum_k x[b,c,l*stride-pad+k*dil] * w[c,k] (+ bias[c]), fp32
+ * accumulation in tap order.  x [B][C][lin], w [C][ksize], y [B][C][lout],
+ * all contiguous.  Replaces depthwise_conv1d_kernel
+ * (batch_invariant_ops.py:435-494, launch :531-564). */
+BIO_API int bio_depthwise_conv1d(int32_t dtype, const void* x, const void* w, const void* bias,
+                                 void* y, int64_t batch, int64_t channels, int64_t lin,
+                                 int64_t lout, int32_t ksize, int32_t stride, int32_t padding,
+                                 int32_t dilation, int32_t device, void* stream);
+
+/* Layout transform of a non-overlapping transposed convolution: src is the
+ * per-(sample, group) GEMM result [B][G][Og*kvol][prod(in)], dst is
+ * [B][G*Og][in0*k0][in1*k1][in2*k2]; dst = src (+ bias[channel]).  Replaces
+ * the bias add and pixel-shuffle permute of conv_transpose2d/3d_batch_invariant
+ * (batch_invariant_ops.py:846-861, 926-941). */
+BIO_API int bio_conv_transpose_scatter(int32_t dtype, const void* src, const void* bias,
+                                       void* dst, const bio_conv_geom* geom,
+                                       int64_t out_channels_per_group, int32_t device,
+                                       void* stream);
+
+/* ---- attention ------------------------------------------------------------
+ * Fused attention, one warp per (sequence, head, query row), keys visited in
+ * fixed blocks of 32 in order with an online softmax in fp32; a row's bits do
+ * not depend on the other rows, sequences or heads of the launch.  Tensors are
+ * [batch][head][token][dim] through element strides (dim contiguous); KV head
+ * of query head h is h / (heads / kv_heads).  Fully masked rows and empty KV
+ * ranges produce zeros.  d, dv <= 256. */
+#define BIO_MASK_NONE 0
+#define BIO_MASK_BOOL 1 /* uint8/bool keep-mask: 0 drops the key           */
+#define BIO_MASK_ADD 2  /* additive float mask in mask_dtype                */
+
+#define BIO_CAUSAL_NONE 0
+#define BIO_CAUSAL_TOP_LEFT 1     /* key j visible iff j <= i                  */
+#define BIO_CAUSAL_BOTTOM_RIGHT 2 /* key j visible iff j <= i + (lk - lq)     */
+#define BIO_CAUSAL_EQUAL 3        /* top-left; varlen requires lq == lk       */
+
+typedef struct bio_attn_args {
+  int32_t dtype;
+  int32_t device;
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t q_sb, q_sh, q_st;
+  int64_t k_sb, k_sh, k_st;
+  int64_t v_sb, v_sh, v_st;
+  int64_t o_sb, o_sh, o_st;
+  int64_t batch, heads, kv_heads;
+  int64_t lq, lk;      /* varlen: total packed query / key tokens          */
+  int32_t d, dv;
+  float scale;
+  int32_t causal;      /* BIO_CAUSAL_*                                      */
+  int32_t mask_kind;   /* BIO_MASK_* (dense only)                           */
+  int32_t mask_dtype;  /* BIO_F32/F16/BF16 for BIO_MASK_ADD                 */
+  const void* mask;    /* element (b, h, i, j) at b*m_sb + h*m_sh + i*m_sq + j*m_sk */
+  int64_t m_sb, m_sh, m_sq, m_sk;
+  const void* cu_q;    /* varlen: [nseq + 1] offsets (int32 or int64)      */
+  const void* cu_k;
+  int32_t cu_is64;
+  int64_t nseq;
+} bio_attn_args;
+
+/* Dense SDPA over [batch][heads][lq|lk][d|dv].  Replaces
+ * scaled_dot_product_attention_batch_invariant (batch_invariant_ops.py:1148-1213). */
+BIO_API int bio_attention(const bio_attn_args* args, void* stream);
+
+/* Sequence-packed attention: q [lq tokens][heads][d], k/v [lk tokens][kv_heads]
+ * (batch strides ignored); sequence s covers query tokens [cu_q[s], cu_q[s+1])
+ * and keys [cu_k[s], cu_k[s+1]); query tokens outside every sequence are
+ * written as zeros.  Offsets are read on the device (no host sync); invalid
+ * offsets raise BIO_DEV_INDEX and zero the affected rows.  Replaces
+ * varlen_scaled_dot_product_attention_batch_invariant
+ * (batch_invariant_ops.py:1216-1344). */
+BIO_API int bio_attention_varlen(const bio_attn_args* args, void* stream);
+
+/* ---- mixture of experts ---------------------------------------------------
+ * The expert GEMMs themselves run through bio_gemm (one fixed-schedule GEMM
+ * per expert, tokens broadcast with a stride-0 batch). */
+
+/* act[i] = silu(gate[i]) * up[i] over n contiguous elements, silu rounded to
+ * the dtype before the product (the reference's F.silu(gate) * up,
+ * batch_invariant_ops/moe.py:79). */
+BIO_API int bio_silu_mul(int32_t dtype, const void* gate, const void* up, void* out, int64_t n,
+                         int32_t device, void* stream);
+
+/* out[t, :] = sum_{j=0..top_k-1} (left to right) expert_out[sel[t,j], t, :] *
+ * w[t, j], each product and partial sum rounded to dtype.  expert_out
+ * [experts][tokens][hidden], w [tokens][top_k] in w_dtype, sel int64
+ * [tokens][top_k], out [tokens][hidden], all contiguous.  Out-of-range expert
+ * ids raise BIO_DEV_INDEX and zero the row.  Replaces the gather / weight /
+ * route-sum chain of deterministic_token_choice_moe (moe.py:67-92). */
+BIO_API int bio_moe_route_sum(int32_t dtype, const void* expert_out, int32_t w_dtype,
+                              const void* routing_weights, const int64_t* selected_experts,
+                              void* out, int64_t experts, int64_t tokens, int64_t top_k,
+                              int64_t hidden, int32_t device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

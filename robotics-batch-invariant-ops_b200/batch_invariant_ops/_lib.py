@@ -89,6 +89,19 @@ SIGNATURES: dict[str, tuple] = {
     "bio_gemm_tile_config": (ctypes.c_int, [_I64, _I64, _I32]),
     "bio_softmax": (ctypes.c_int, [_I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "bio_reduce": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _P]),
+    "bio_im2col": (ctypes.c_int, [_I32, _P, _P, _P, _I64, _I32, _P]),
+    "bio_depthwise_conv1d": (
+        ctypes.c_int,
+        [_I32, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _P],
+    ),
+    "bio_conv_transpose_scatter": (ctypes.c_int, [_I32, _P, _P, _P, _P, _I64, _I32, _P]),
+    "bio_attention": (ctypes.c_int, [_P, _P]),
+    "bio_attention_varlen": (ctypes.c_int, [_P, _P]),
+    "bio_silu_mul": (ctypes.c_int, [_I32, _P, _P, _P, _I64, _I32, _P]),
+    "bio_moe_route_sum": (
+        ctypes.c_int,
+        [_I32, _P, _I32, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
+    ),
     "bio_pack_rows": (
         ctypes.c_int,
         [_I32, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I32, _P],

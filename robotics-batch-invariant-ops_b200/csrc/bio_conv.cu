@@ -1,0 +1,264 @@
+// Convolution lowering kernels.
+//
+// * bio_im2col: gathers the receptive fields of an N-d (N <= 3) convolution
+//   into a dense [B][G][L][Kpad] patch matrix (K = C/G * kernel volume, zero
+//   padded to Kpad); the GEMM then computes out[b, g] = W_g [Og, K] x
+//   patches[b, g]^T, one independent fixed-schedule GEMM per (sample, group),
+//   so a sample's output never depends on the other samples.
+// * bio_depthwise_conv1d: direct depthwise kernel, fp32 accumulation over the
+//   taps in order k = 0..K-1, bias added after the taps.
+// * bio_conv_transpose_scatter: pixel-shuffle layout transform (+ bias) of the
+//   per-(sample, group) GEMM output of a non-overlapping transposed
+//   convolution (stride == kernel).
+//
+// Reference: conv1d_batch_invariant (batch_invariant_ops.py:497-595, depthwise
+// kernel :435-494), conv2d_batch_invariant (:598-682), conv3d_batch_invariant
+// (:685-780), conv_transpose2d/3d_batch_invariant (:783-941).
+#include "bio_common.cuh"
+
+namespace bio {
+
+struct Geom {
+  int64_t batch, channels, groups;
+  int64_t in[3], kernel[3], stride[3], padding[3], dilation[3], out[3];
+};
+
+template <typename T>
+__global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ patches, Geom g,
+                              int64_t k_real, int64_t kpad, int64_t total) {
+  const int64_t kvol = g.kernel[0] * g.kernel[1] * g.kernel[2];
+  const int64_t L = g.out[0] * g.out[1] * g.out[2];
+  const int64_t cg = g.channels / g.groups;
+  const int64_t in_vol = g.in[0] * g.in[1] * g.in[2];
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t kk = idx % kpad;
+    int64_t rest = idx / kpad;
+    const int64_t l = rest % L;
+    rest /= L;
+    const int64_t grp = rest % g.groups;
+    const int64_t b = rest / g.groups;
+    T v = from_f32<T>(0.f);
+    if (kk < k_real) {
+      const int64_t c = kk / kvol;
+      int64_t z = kk - c * kvol;
+      const int64_t z2 = z % g.kernel[2];
+      z /= g.kernel[2];
+      const int64_t z1 = z % g.kernel[1];
+      const int64_t z0 = z / g.kernel[1];
+      const int64_t o2 = l % g.out[2];
+      const int64_t t = l / g.out[2];
+      const int64_t o1 = t % g.out[1];
+      const int64_t o0 = t / g.out[1];
+      const int64_t i0 = o0 * g.stride[0] - g.padding[0] + z0 * g.dilation[0];
+      const int64_t i1 = o1 * g.stride[1] - g.padding[1] + z1 * g.dilation[1];
+      const int64_t i2 = o2 * g.stride[2] - g.padding[2] + z2 * g.dilation[2];
+      if (i0 >= 0 && i0 < g.in[0] && i1 >= 0 && i1 < g.in[1] && i2 >= 0 && i2 < g.in[2]) {
+        const int64_t ch = grp * cg + c;
+        v = x[(b * g.channels + ch) * in_vol + (i0 * g.in[1] + i1) * g.in[2] + i2];
+      }
+    }
+    patches[idx] = v;
+  }
+}
+
+template <typename T>
+__global__ void depthwise_conv1d_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                        const T* __restrict__ bias, T* __restrict__ y,
+                                        int64_t channels, int64_t lin, int64_t lout, int ksize,
+                                        int stride, int pad, int dil, int64_t total) {
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t l = idx % lout;
+    const int64_t bc = idx / lout;
+    const int64_t c = bc % channels;
+    const T* xr = x + bc * lin;
+    const T* wr = w + c * ksize;
+    float acc = 0.f;
+    for (int k = 0; k < ksize; ++k) {
+      const int64_t i = l * stride - pad + static_cast<int64_t>(k) * dil;
+      if (i >= 0 && i < lin) acc += to_f32(xr[i]) * to_f32(wr[k]);
+    }
+    if (bias != nullptr) acc += to_f32(bias[c]);
+    y[idx] = from_f32<T>(acc);
+  }
+}
+
+// dst[b, g*Og + o, s*k + z ...] = src[b, g, o*kvol + z, s] (+ bias[g*Og + o])
+template <typename T>
+__global__ void convt_scatter_kernel(const T* __restrict__ src, const T* __restrict__ bias,
+                                     T* __restrict__ dst, Geom g, int64_t og, int64_t total) {
+  const int64_t k0 = g.kernel[0], k1 = g.kernel[1], k2 = g.kernel[2];
+  const int64_t s0 = g.in[0], s1 = g.in[1], s2 = g.in[2];
+  const int64_t d1 = s1 * k1, d2 = s2 * k2;
+  const int64_t out_vol = s0 * k0 * d1 * d2;
+  const int64_t in_vol = s0 * s1 * s2;
+  const int64_t kvol = k0 * k1 * k2;
+  const int64_t cout = og * g.groups;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t pos = idx % out_vol;
+    const int64_t bc = idx / out_vol;
+    const int64_t oc = bc % cout;
+    const int64_t b = bc / cout;
+    const int64_t p2 = pos % d2;
+    pos /= d2;
+    const int64_t p1 = pos % d1;
+    const int64_t p0 = pos / d1;
+    const int64_t i0 = p0 / k0, z0 = p0 - i0 * k0;
+    const int64_t i1 = p1 / k1, z1 = p1 - i1 * k1;
+    const int64_t i2 = p2 / k2, z2 = p2 - i2 * k2;
+    const int64_t grp = oc / og, o = oc - grp * og;
+    const int64_t q = o * kvol + (z0 * k1 + z1) * k2 + z2;
+    const int64_t i = (i0 * s1 + i1) * s2 + i2;
+    float v = to_f32(src[((b * g.groups + grp) * og * kvol + q) * in_vol + i]);
+    if (bias != nullptr) v += to_f32(bias[oc]);
+    dst[idx] = from_f32<T>(v);
+  }
+}
+
+}  // namespace bio
+
+namespace {
+
+bio::Geom to_geom(const bio_conv_geom* c) {
+  bio::Geom g;
+  g.batch = c->batch;
+  g.channels = c->channels;
+  g.groups = c->groups;
+  for (int i = 0; i < 3; ++i) {
+    g.in[i] = c->in[i];
+    g.kernel[i] = c->kernel[i];
+    g.stride[i] = c->stride[i];
+    g.padding[i] = c->padding[i];
+    g.dilation[i] = c->dilation[i];
+    g.out[i] = c->out[i];
+  }
+  return g;
+}
+
+unsigned blocks_for(int64_t total) {
+  int64_t b = (total + 255) / 256;
+  if (b > 65536 * 4) b = 65536 * 4;
+  return static_cast<unsigned>(b);
+}
+
+bool geom_ok(const bio_conv_geom* c) {
+  if (c == nullptr) return false;
+  if (c->batch < 0 || c->channels <= 0 || c->groups <= 0 || c->channels % c->groups) return false;
+  for (int i = 0; i < 3; ++i) {
+    if (c->in[i] < 1 || c->kernel[i] < 1 || c->stride[i] < 1 || c->dilation[i] < 1) return false;
+    if (c->padding[i] < 0 || c->out[i] < 0) return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bio_im2col(int32_t dtype, const void* x, const bio_conv_geom* geom, void* patches,
+               int64_t kpad, int32_t device, void* stream) {
+  if (!geom_ok(geom)) return BIO_ERR_SHAPE;
+  const int64_t cg = geom->channels / geom->groups;
+  const int64_t k_real = cg * geom->kernel[0] * geom->kernel[1] * geom->kernel[2];
+  if (kpad < k_real) return BIO_ERR_SHAPE;
+  const int64_t L = geom->out[0] * geom->out[1] * geom->out[2];
+  const int64_t total = geom->batch * geom->groups * L * kpad;
+  if (total == 0) return BIO_OK;
+  if (x == nullptr || patches == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bio::Geom g = to_geom(geom);
+  switch (dtype) {
+    case BIO_F32:
+      bio::im2col_kernel<float><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const float*>(x), static_cast<float*>(patches), g, k_real, kpad, total);
+      break;
+    case BIO_F16:
+      bio::im2col_kernel<__half><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const __half*>(x), static_cast<__half*>(patches), g, k_real, kpad, total);
+      break;
+    case BIO_BF16:
+      bio::im2col_kernel<__nv_bfloat16><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(patches), g, k_real,
+          kpad, total);
+      break;
+    default: return BIO_ERR_DTYPE;
+  }
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+int bio_depthwise_conv1d(int32_t dtype, const void* x, const void* w, const void* bias, void* y,
+                         int64_t batch, int64_t channels, int64_t lin, int64_t lout,
+                         int32_t ksize, int32_t stride, int32_t padding, int32_t dilation,
+                         int32_t device, void* stream) {
+  if (batch < 0 || channels < 0 || lin < 0 || lout < 0 || ksize < 1 || stride < 1 ||
+      dilation < 1 || padding < 0)
+    return BIO_ERR_SHAPE;
+  const int64_t total = batch * channels * lout;
+  if (total == 0) return BIO_OK;
+  if (x == nullptr || w == nullptr || y == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case BIO_F32:
+      bio::depthwise_conv1d_kernel<float><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const float*>(x), static_cast<const float*>(w),
+          static_cast<const float*>(bias), static_cast<float*>(y), channels, lin, lout, ksize,
+          stride, padding, dilation, total);
+      break;
+    case BIO_F16:
+      bio::depthwise_conv1d_kernel<__half><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const __half*>(x), static_cast<const __half*>(w),
+          static_cast<const __half*>(bias), static_cast<__half*>(y), channels, lin, lout, ksize,
+          stride, padding, dilation, total);
+      break;
+    case BIO_BF16:
+      bio::depthwise_conv1d_kernel<__nv_bfloat16><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+          static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y), channels, lin,
+          lout, ksize, stride, padding, dilation, total);
+      break;
+    default: return BIO_ERR_DTYPE;
+  }
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+int bio_conv_transpose_scatter(int32_t dtype, const void* src, const void* bias, void* dst,
+                               const bio_conv_geom* geom, int64_t out_channels_per_group,
+                               int32_t device, void* stream) {
+  if (!geom_ok(geom) || out_channels_per_group < 1) return BIO_ERR_SHAPE;
+  const int64_t out_vol = geom->in[0] * geom->kernel[0] * geom->in[1] * geom->kernel[1] *
+                          geom->in[2] * geom->kernel[2];
+  const int64_t total = geom->batch * geom->groups * out_channels_per_group * out_vol;
+  if (total == 0) return BIO_OK;
+  if (src == nullptr || dst == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bio::Geom g = to_geom(geom);
+  switch (dtype) {
+    case BIO_F32:
+      bio::convt_scatter_kernel<float><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const float*>(src), static_cast<const float*>(bias),
+          static_cast<float*>(dst), g, out_channels_per_group, total);
+      break;
+    case BIO_F16:
+      bio::convt_scatter_kernel<__half><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const __half*>(src), static_cast<const __half*>(bias),
+          static_cast<__half*>(dst), g, out_channels_per_group, total);
+      break;
+    case BIO_BF16:
+      bio::convt_scatter_kernel<__nv_bfloat16><<<blocks_for(total), 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(src), static_cast<const __nv_bfloat16*>(bias),
+          static_cast<__nv_bfloat16*>(dst), g, out_channels_per_group, total);
+      break;
+    default: return BIO_ERR_DTYPE;
+  }
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+}  // extern "C"

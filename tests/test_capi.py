@@ -76,3 +76,38 @@ def test_gemm_rejects_bad_arguments_without_gpu():
     args.batch2 = 0
     assert lib.bio_gemm(ctypes.byref(args), None) == _lib.BIO_ERR_SHAPE
     assert lib.bio_gemm(None, None) == _lib.BIO_ERR_ARG
+
+
+def test_struct_layouts_match_the_c_header(tmp_path):
+    """Compile a C probe against include/bio_sm100.h and compare sizeof/offsets
+    of every ABI struct with the ctypes mirrors."""
+    import shutil
+    import subprocess
+
+    from batch_invariant_ops import _attn, _conv
+
+    gcc = shutil.which("gcc") or shutil.which("cc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    mirrors = {
+        "bio_gemm_args": _lib.GemmArgs,
+        "bio_attn_args": _attn._AttnArgs,
+        "bio_conv_geom": _conv._Geom,
+    }
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){"]
+    for cname, py in mirrors.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            cfield = {"inp": "in"}.get(fname, fname)
+            lines.append(f'printf("{cname}.{fname} %zu\\n", offsetof({cname}, {cfield}));')
+    lines.append("return 0;}")
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run([gcc, str(src), "-o", str(exe)], check=True)
+    got = dict(l.rsplit(" ", 1) for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                         check=True).stdout.splitlines())
+    for cname, py in mirrors.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
