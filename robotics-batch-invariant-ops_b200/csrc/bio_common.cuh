@@ -2,7 +2,7 @@
 //
 // Device side: thin inline-PTX wrappers for mbarriers, TMA (cp.async.bulk
 // .tensor), tcgen05 (TMEM alloc, MMA, commit, ld) and bounded waits.  Every
-// spin-wait in this library goes through `bounded_wait`, which gives up after
+// spin-wait in this library goes through `mbar_wait`, which gives up after
 // kWaitTimeoutNs (globaltimer) or kWaitMaxIters polls, raises BIO_DEV_TIMEOUT
 // in the device status word and lets the kernel unwind instead of hanging.
 //
