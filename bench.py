@@ -11,8 +11,10 @@ Reported (one JSON line from rank 0):
   value     whole-job TFLOP/s = sum of 2*M*N*K over all points and ranks /
             max over ranks of the summed device time of the GEMM launches.
             Each launch is replayed from a CUDA graph and bracketed by CUDA
-            events on its stream; a 512 MiB write flushes L2 between launches
-            (outside the events), so no operand is L2-resident.
+            events on its stream; between launches (outside the events) a
+            512 MiB write flushes L2 and a 256 MiB read then evicts the dirty
+            lines, so no operand is L2-resident and the timed kernel does not
+            pay for the flush's write-backs.
   e2e       the same metric through the public Python API with the step's
             activations copied host->device from pinned memory and the
             outputs copied back, inside the timed region.
@@ -55,6 +57,7 @@ SWEEP_N = (4096, 11008, 16384)
 SWEEP_M = (1, 8, 32, 128, 512, 2048, 8192)
 K = 4096
 FLUSH_BYTES = 512 << 20
+EVICT_BYTES = 256 << 20
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -137,6 +140,22 @@ class ClockSampler:
         }
 
 
+class _Flusher:
+    """L2 flush between timed launches: write FLUSH_BYTES, then read EVICT_BYTES
+    of another buffer so the written lines are evicted (written back) before
+    the next timed launch starts."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.w = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(EVICT_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
+
 # ---------------------------------------------------------------------------
 # distributed helpers
 # ---------------------------------------------------------------------------
@@ -208,7 +227,7 @@ def run_ours(args) -> None:
         w = (torch.randn(n, K, device=dev, generator=gen) / 64).to(torch.bfloat16)
         b = (torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
         weights[n] = (w, b)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = _Flusher(dev)
     points = _points()
     stream = torch.cuda.current_stream(dev)
 
@@ -234,7 +253,7 @@ def run_ours(args) -> None:
     def device_step(record):
         evs = []
         for p in points:
-            flush.zero_()
+            flush()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
@@ -284,7 +303,7 @@ def run_ours(args) -> None:
     def e2e_step(record):
         evs = []
         for m, n in points:
-            flush.zero_()
+            flush()
             w, b = weights[n]
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
@@ -392,7 +411,7 @@ def run_ours(args) -> None:
                 "N": list(SWEEP_N),
                 "M": list(SWEEP_M),
                 "layout": "F.linear: weight [N,K] K-contiguous",
-                "l2": "flushed (512 MiB write) before every timed launch, outside the events",
+                "l2": "flushed before every timed launch (512 MiB write + 256 MiB read), outside the events",
                 "timing": "CUDA graph replay per point, CUDA events on the launch stream",
                 "parallelism": f"replica{world} (each rank runs the full sweep)",
             },
@@ -452,7 +471,7 @@ def run_triton_ref_worker(args) -> None:
         w = (torch.randn(n, K, device=dev, generator=gen) / 64).to(torch.bfloat16)
         b = (torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
         weights[n] = (w, b)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = _Flusher(dev)
     points = _points()
     stream = torch.cuda.current_stream(dev)
     for m, n in points:
@@ -468,7 +487,7 @@ def run_triton_ref_worker(args) -> None:
     for step in range(max(args.warmup, 3) + args.steps):
         evs = []
         for p in points:
-            flush.zero_()
+            flush()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             graphs[p].replay()

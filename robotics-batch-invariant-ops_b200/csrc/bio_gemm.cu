@@ -31,7 +31,7 @@ constexpr int kGemmThreads = 192;
 
 struct TcGemmParams {
   int m, n, k;
-  int tiles_m, tiles_n, k_blocks;
+  int tiles_m, tiles_n, k_blocks, group_m;
   int64_t batch2;
   int64_t total_tiles;
   int a_div2, b_div2;
@@ -51,19 +51,19 @@ struct TileIdx {
   int mb, nb;
 };
 
-// Tile t -> (batch, m-block, n-block).  Grouped raster (8 m-blocks sweep the
-// n-blocks) for L2 reuse; the order only affects which CTA computes a tile,
-// never the arithmetic of the tile.
+// Tile t -> (batch, m-block, n-block).  Grouped raster: a group of `group_m`
+// m-blocks (sized on the host so the group's A panel stays in L2) sweeps all
+// n-blocks, so each B panel is streamed once per group.  The order only
+// decides which CTA computes a tile, never the arithmetic of the tile.
 __device__ __forceinline__ TileIdx decode_tile(int64_t t, int tiles_m, int tiles_n,
-                                               int64_t batch2) {
+                                               int64_t batch2, int group_m) {
   const int64_t per = static_cast<int64_t>(tiles_m) * tiles_n;
   const int64_t bi = t / per;
   const int r = static_cast<int>(t - bi * per);
-  constexpr int kGroupM = 8;
-  const int in_group = kGroupM * tiles_n;
+  const int in_group = group_m * tiles_n;
   const int g = r / in_group;
-  const int first_m = g * kGroupM;
-  const int gsz = min(tiles_m - first_m, kGroupM);
+  const int first_m = g * group_m;
+  const int gsz = min(tiles_m - first_m, group_m);
   const int rr = r - g * in_group;
   TileIdx ti;
   ti.mb = first_m + rr % gsz;
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
-        const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2);
+        const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
         const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
         const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
         const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     const T* bias = static_cast<const T*>(p.bias);
     for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
-      const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2);
+      const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
@@ -341,6 +341,257 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Paired (cta_group::2) tensor-core GEMM: a cluster of two CTAs on two SMs
+// computes a 256 x BN tile with M=256 tcgen05.mma issued by the leader CTA.
+// CTA r loads rows [r*128, r*128+128) of the A tile and rows
+// [r*BN/2, r*BN/2 + BN/2) of the B tile into its own shared memory (plain
+// TMA, no multicast); the transaction bytes of both land on the leader's
+// stage barrier.  Each CTA's TMEM holds its 128 output rows x BN fp32
+// columns; each CTA's epilogue stores its own rows.  Per SM this halves the
+// B bytes per flop against the single-CTA 128 x BN tile.
+//
+// Arithmetic per output element is the same fixed sequence as the
+// single-CTA kernel family's contract: k-block 0..K/64-1, four K=16 MMAs in
+// order; the instruction shape (M=256, N=BN) is a function of (N, K, dtype).
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES>
+struct Tc2Smem {
+  static constexpr uint32_t kABytes = 128 * kBK * 2;
+  static constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarBytes = (2 * STAGES + 5) * 8 + 16;
+  static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kBarBytes;
+};
+
+// Bounded spin on the global timer (used only on the abort path so that copies
+// still in flight land before the CTA releases its shared memory).
+__device__ __forceinline__ void grace_spin_ns(uint64_t ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (global_timer_ns() - t0 < ns) {
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB, const TcGemmParams p) {
+  using L = Tc2Smem<BN, STAGES>;
+  constexpr int BNH = BN / 2;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc = idesc_f16(TypeFmt<T>::umma, 256, BN, A_MN, B_MN);
+  constexpr uint32_t kBoxBytesMN = 64 * kBK * 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * L::kBBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* mma_done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 8);
+    }
+    mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(tmem_slot, kTmemCols);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < p.total_tiles; t += npairs) {
+        const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+        const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
+        const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
+        const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int a_row = ti.mb * 256 + static_cast<int>(rank) * 128;
+        const int b_row = ti.nb * BN + static_cast<int>(rank) * BNH;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * L::kABytes;
+          uint8_t* b_dst = sB + stage * L::kBBytes;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+          const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if constexpr (!A_MN) {
+            tma_load_4d_2sm(a_dst, &tmA, bar, kb * kBK, a_row, a2, a1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              tma_load_4d_2sm(a_dst + j * kBoxBytesMN, &tmA, bar, a_row + j * 64, kb * kBK, a2, a1);
+          }
+          if constexpr (!B_MN) {
+            tma_load_4d_2sm(b_dst, &tmB, bar, kb * kBK, b_row, b2, b1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BNH / 64; ++j)
+              tma_load_4d_2sm(b_dst + j * kBoxBytesMN, &tmB, bar, b_row + j * 64, kb * kBK, b2, b1);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------ MMA issuer (leader CTA only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < p.total_tiles; t += npairs) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? smem_desc_sw128(a_addr + kk * 2048, kBoxBytesMN, 1024)
+                                        : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 2048, kBoxBytesMN, 1024)
+                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_2sm(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_2sm_mc(&empty_bar[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_2sm_mc(&tfull_bar[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit_2sm(mma_done_bar);
+      if (!mbar_wait_drain(mma_done_bar, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else {
+    // -------------------------------- epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const T* bias = static_cast<const T*>(p.bias);
+    for (int64_t t = pair; t < p.total_tiles; t += npairs) {
+      const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+      const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
+                static_cast<int64_t>(m) * p.c_sm;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) +
+                               (static_cast<uint32_t>(q * 32) << 16),
+                           r);
+        tmem_ld_wait();
+        const int n0 = ti.nb * BN + c0;
+        if (m < p.m && n0 < p.n) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+          if (bias != nullptr) {
+            const T* bb = bias + ti.b2 * p.bias_s2;
+            if (p.bias_per_row) {
+              const float bv = to_f32(bb[m]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += bv;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.n) v[j] += to_f32(bb[n0 + j]);
+            }
+          }
+          if (p.c_vec_ok && n0 + 32 <= p.n) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+              w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+              w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+              w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+              dst[j] = w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // Abort path: give loads already issued (which count on the leader's
+  // barriers) a bounded time to land before shared memory is released.
+  if (threadIdx.x == 0 && *abort_flag) grace_spin_ns(200000);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem_base, kTmemCols);
   }
 }
 
@@ -613,35 +864,83 @@ int encode_map(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md, 
   return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
 }
 
-// Tile N chosen from (n, k, dtype) only.  Wide N tiles for wide outputs (more
-// reuse of A per byte of B), narrow ones for narrow outputs so that even a
-// single row (M = 1) spreads the weight stream over many SMs.
-int pick_bn(int64_t n, int64_t /*k*/, int32_t /*dtype*/) {
-  if (n >= 32768) return 256;
-  if (n >= 8192) return 128;
-  return 64;
+// Tile chosen from (n, k, dtype) only -- never from m or the batch count:
+//   n <= 64      single-CTA 128 x 64 tile
+//   n <  8192    CTA pair, 256 x 128 tile (64 B rows per SM)
+//   otherwise    CTA pair, 256 x 256 tile (128 B rows per SM)
+// Narrow N tiles for narrow outputs keep the weight stream of a single row
+// (m = 1) spread over many SMs; the pair halves B bytes per flop per SM.
+struct TileChoice {
+  bool pair;
+  int bn;
+};
+
+TileChoice pick_tile(int64_t n, int64_t /*k*/, int32_t /*dtype*/) {
+  if (n <= 64) return {false, 64};
+  if (n < 8192) return {true, 128};
+  return {true, 256};
 }
 
-template <int BN>
+template <bool PAIR, int BN>
 constexpr int stages_for() {
+  if (PAIR) return BN == 128 ? 8 : 6;
   return BN == 64 ? 8 : (BN == 128 ? 6 : 4);
 }
 
 std::mutex g_attr_mu;
 
-template <int BN, bool A_MN, bool B_MN, typename T>
+template <bool PAIR, int BN, int STAGES>
+constexpr uint32_t smem_bytes() {
+  return PAIR ? bio::Tc2Smem<BN, STAGES>::kTotal : bio::TcSmem<BN, STAGES>::kTotal;
+}
+
+// Rows of A a group of the raster may hold so that the group's A panel
+// (group * BM * K * 2 bytes) stays within ~48 MB of L2.
+int group_rows(int64_t k, int bm, int tiles_m) {
+  const int64_t panel = static_cast<int64_t>(bm) * k * 2;
+  int64_t g = panel > 0 ? (48ll << 20) / panel : tiles_m;
+  if (g < 1) g = 1;
+  if (g > tiles_m) g = tiles_m;
+  return static_cast<int>(g);
+}
+
+template <bool PAIR, int BN, bool A_MN, bool B_MN, typename T>
 int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
-  constexpr int STAGES = stages_for<BN>();
-  using L = bio::TcSmem<BN, STAGES>;
-  auto kern = bio::gemm_tc_kernel<BN, STAGES, A_MN, B_MN, T>;
+  constexpr int STAGES = stages_for<PAIR, BN>();
+  constexpr uint32_t kSmem = smem_bytes<PAIR, BN, STAGES>();
+  constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
+  constexpr int kBoxARows = PAIR ? 128 : kBM;     // A rows each CTA loads
+  constexpr int kBoxBRows = PAIR ? BN / 2 : BN;   // B rows each CTA loads
+  auto kern = PAIR ? bio::gemm_tc2_kernel<BN, STAGES, A_MN, B_MN, T>
+                   : bio::gemm_tc_kernel<BN, STAGES, A_MN, B_MN, T>;
 
   static bool attr_done[bio_host::kMaxDevices] = {false};
+  static int max_units[bio_host::kMaxDevices] = {0};
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
     if (!attr_done[a->device]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
           cudaSuccess)
         return BIO_ERR_LAUNCH;
+      int units = bio_host::sm_count(a->device);
+      if (PAIR) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * 74, 1, 1);
+        cfg.blockDim = dim3(bio::kGemmThreads, 1, 1);
+        cfg.dynamicSmemBytes = kSmem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+          clusters = units / 2;
+        units = clusters;
+      }
+      max_units[a->device] = units;
       attr_done[a->device] = true;
     }
   }
@@ -669,19 +968,20 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   }
   CUtensorMap tmA, tmB;
   int st = A_MN ? encode_map(&tmA, a->dtype, a->a, ma, 64, kBK)
-                : encode_map(&tmA, a->dtype, a->a, ma, kBK, kBM);
+                : encode_map(&tmA, a->dtype, a->a, ma, kBK, kBoxARows);
   if (st != BIO_OK) return st;
   st = B_MN ? encode_map(&tmB, a->dtype, a->b, mb, 64, kBK)
-            : encode_map(&tmB, a->dtype, a->b, mb, kBK, BN);
+            : encode_map(&tmB, a->dtype, a->b, mb, kBK, kBoxBRows);
   if (st != BIO_OK) return st;
 
   bio::TcGemmParams p;
   p.m = static_cast<int>(a->m);
   p.n = static_cast<int>(a->n);
   p.k = static_cast<int>(a->k);
-  p.tiles_m = static_cast<int>((a->m + kBM - 1) / kBM);
+  p.tiles_m = static_cast<int>((a->m + kTileM - 1) / kTileM);
   p.tiles_n = static_cast<int>((a->n + BN - 1) / BN);
   p.k_blocks = static_cast<int>((a->k + kBK - 1) / kBK);
+  p.group_m = group_rows(a->k, kTileM, p.tiles_m);
   p.batch2 = a->batch2;
   p.total_tiles = batch * p.tiles_m * p.tiles_n;
   p.a_div2 = static_cast<int>(a->a_div2);
@@ -705,20 +1005,20 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
                    : 0;
   p.status = bio_host::status_word(a->device);
 
-  const int sms = bio_host::sm_count(a->device);
-  if (sms <= 0) return BIO_ERR_LAUNCH;
-  const int64_t grid = p.total_tiles < sms ? p.total_tiles : sms;
-  kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, L::kTotal, stream>>>(tmA, tmB, p);
+  const int64_t units = max_units[a->device];
+  if (units <= 0) return BIO_ERR_LAUNCH;
+  const int64_t n_units = p.total_tiles < units ? p.total_tiles : units;
+  const int64_t grid = PAIR ? 2 * n_units : n_units;
+  kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, p);
   return bio_host::launch_status(cudaGetLastError());
 }
 
 template <bool A_MN, bool B_MN, typename T>
 int dispatch_bn(const bio_gemm_args* a, cudaStream_t stream) {
-  switch (pick_bn(a->n, a->k, a->dtype)) {
-    case 64: return launch_tc<64, A_MN, B_MN, T>(a, stream);
-    case 128: return launch_tc<128, A_MN, B_MN, T>(a, stream);
-    default: return launch_tc<256, A_MN, B_MN, T>(a, stream);
-  }
+  const TileChoice tc = pick_tile(a->n, a->k, a->dtype);
+  if (!tc.pair) return launch_tc<false, 64, A_MN, B_MN, T>(a, stream);
+  if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, stream);
+  return launch_tc<true, 256, A_MN, B_MN, T>(a, stream);
 }
 
 template <typename T>
@@ -787,7 +1087,8 @@ extern "C" {
 
 int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype) {
   if (dtype == BIO_F32) return bio::kF32BM * 1000000 + bio::kF32BN * 1000 + bio::kF32BK;
-  return kBM * 1000000 + pick_bn(n, k, dtype) * 1000 + kBK;
+  const TileChoice tc = pick_tile(n, k, dtype);
+  return (tc.pair ? 256 : kBM) * 1000000 + tc.bn * 1000 + kBK;
 }
 
 int bio_gemm(const bio_gemm_args* a, void* stream_v) {
