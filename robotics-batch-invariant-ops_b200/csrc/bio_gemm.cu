@@ -32,6 +32,10 @@ constexpr int kGemmThreads = 192;
 struct TcGemmParams {
   int m, n, k;
   int tiles_m, tiles_n, k_blocks, group_m;
+  // paired kernel: runtime ring depth, byte stride between A stages and the
+  // row count of the tail box (valid rows of a partial 128-row A slab,
+  // rounded up to 8); 0 when M is a multiple of 128.
+  int stages, a_stride, a_tail_rows;
   int64_t batch2;
   int64_t total_tiles;
   int a_div2, b_div2;
@@ -358,13 +362,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // single-CTA kernel family's contract: k-block 0..K/64-1, four K=16 MMAs in
 // order; the instruction shape (M=256, N=BN) is a function of (N, K, dtype).
 // ---------------------------------------------------------------------------
+constexpr int kMaxStages2 = 32;
+
+// Shared memory of the paired kernel: a data region sized for STAGES full
+// stages (A 128x64 + B (BN/2)x64), then the barriers.  At run time the ring
+// may use a denser A stride (small M, see TcGemmParams::a_stride) and more
+// stages in the same data region.
 template <int BN, int STAGES>
 struct Tc2Smem {
   static constexpr uint32_t kABytes = 128 * kBK * 2;
   static constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kBarBytes = (2 * STAGES + 5) * 8 + 16;
-  static constexpr uint32_t kTotal = 1024 + STAGES * kStageBytes + kBarBytes;
+  static constexpr uint32_t kData = STAGES * (kABytes + kBBytes);
+  static constexpr uint32_t kBarBytes = (2 * kMaxStages2 + 5) * 8 + 16;
+  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes;
 };
 
 // Bounded spin on the global timer (used only on the abort path so that copies
@@ -375,10 +385,22 @@ __device__ __forceinline__ void grace_spin_ns(uint64_t ns) {
   }
 }
 
+// Bytes of A a CTA loads for a tile: the full 128-row slab, only the valid
+// rows of a partial slab (tail box), or nothing past the end of M.  Rows of
+// the smem slab that are not loaded hold stale data; they only feed output
+// rows >= M, which are never stored (each output row depends on its own A
+// row only), so this changes no stored bit.
+__device__ __forceinline__ uint32_t a_slab_bytes(int valid_rows, int tail_rows) {
+  if (valid_rows >= 128) return 128u * kBK * 2;
+  if (valid_rows <= 0) return 0u;
+  return static_cast<uint32_t>(tail_rows) * kBK * 2;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB, const TcGemmParams p) {
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmA_tail, const TcGemmParams p) {
   using L = Tc2Smem<BN, STAGES>;
   constexpr int BNH = BN / 2;
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -388,11 +410,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int nstages = p.stages;
+  const uint32_t a_stride = static_cast<uint32_t>(p.a_stride);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * L::kABytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * L::kBBytes);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint8_t* sB = smem + nstages * a_stride;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kData);
+  uint64_t* empty_bar = full_bar + kMaxStages2;
+  uint64_t* tfull_bar = empty_bar + kMaxStages2;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* mma_done_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
@@ -406,7 +430,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int64_t npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < nstages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
@@ -446,17 +470,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
         const int a_row = ti.mb * 256 + static_cast<int>(rank) * 128;
         const int b_row = ti.nb * BN + static_cast<int>(rank) * BNH;
+        const int valid0 = p.m - ti.mb * 256;
+        const int my_valid = valid0 - static_cast<int>(rank) * 128;
+        // A_MN operands always move full boxes (zero-filled past M)
+        const uint32_t a0 = A_MN ? L::kABytes : a_slab_bytes(valid0, p.a_tail_rows);
+        const uint32_t a1b = A_MN ? L::kABytes : a_slab_bytes(valid0 - 128, p.a_tail_rows);
+        const uint32_t tx = a0 + a1b + 2 * L::kBBytes;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
             ok = false;
             break;
           }
-          uint8_t* a_dst = sA + stage * L::kABytes;
+          uint8_t* a_dst = sA + stage * a_stride;
           uint8_t* b_dst = sB + stage * L::kBBytes;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx);
           const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if constexpr (!A_MN) {
-            tma_load_4d_2sm(a_dst, &tmA, bar, kb * kBK, a_row, a2, a1);
+            if (my_valid >= 128)
+              tma_load_4d_2sm(a_dst, &tmA, bar, kb * kBK, a_row, a2, a1);
+            else if (my_valid > 0)
+              tma_load_4d_2sm(a_dst, &tmA_tail, bar, kb * kBK, a_row, a2, a1);
           } else {
 #pragma unroll
             for (int j = 0; j < 2; ++j)
@@ -469,7 +502,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < BNH / 64; ++j)
               tma_load_4d_2sm(b_dst + j * kBoxBytesMN, &tmB, bar, b_row + j * 64, kb * kBK, b2, b1);
           }
-          if (++stage == STAGES) {
+          if (++stage == nstages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -494,7 +527,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * L::kABytes);
+          const uint32_t a_addr = smem_u32(sA + stage * a_stride);
           const uint32_t b_addr = smem_u32(sB + stage * L::kBBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
@@ -505,7 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             umma_f16_2sm(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit_2sm_mc(&empty_bar[stage], 0x3);
-          if (++stage == STAGES) {
+          if (++stage == nstages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -866,10 +899,11 @@ int encode_map(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md, 
 
 // Tile chosen from (n, k, dtype) only -- never from m or the batch count:
 //   n <= 64      single-CTA 128 x 64 tile
-//   n <  8192    CTA pair, 256 x 128 tile (64 B rows per SM)
-//   otherwise    CTA pair, 256 x 256 tile (128 B rows per SM)
-// Narrow N tiles for narrow outputs keep the weight stream of a single row
-// (m = 1) spread over many SMs; the pair halves B bytes per flop per SM.
+//   otherwise    CTA pair, 256 x 256 tile (128 A rows + 128 B rows per SM)
+// The 256 x 256 pair tile moves 1/128 byte of operands per flop and SM, which
+// keeps the L2->SM stream below its measured limit at full tensor rate.  Its
+// cost for tiny M is MMA work on padding rows (the instruction shape cannot
+// shrink with M without breaking invariance).
 struct TileChoice {
   bool pair;
   int bn;
@@ -877,7 +911,6 @@ struct TileChoice {
 
 TileChoice pick_tile(int64_t n, int64_t /*k*/, int32_t /*dtype*/) {
   if (n <= 64) return {false, 64};
-  if (n < 8192) return {true, 128};
   return {true, 256};
 }
 
@@ -911,8 +944,12 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
   constexpr int kBoxARows = PAIR ? 128 : kBM;     // A rows each CTA loads
   constexpr int kBoxBRows = PAIR ? BN / 2 : BN;   // B rows each CTA loads
-  auto kern = PAIR ? bio::gemm_tc2_kernel<BN, STAGES, A_MN, B_MN, T>
-                   : bio::gemm_tc_kernel<BN, STAGES, A_MN, B_MN, T>;
+  auto kern = [] {
+    if constexpr (PAIR)
+      return bio::gemm_tc2_kernel<BN, STAGES, A_MN, B_MN, T>;
+    else
+      return bio::gemm_tc_kernel<BN, STAGES, A_MN, B_MN, T>;
+  }();
 
   static bool attr_done[bio_host::kMaxDevices] = {false};
   static int max_units[bio_host::kMaxDevices] = {0};
@@ -966,10 +1003,17 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
                       a->batch1, a->b_s1, a->batch2, a->b_s2, a->b_div2, &mb, &b_b1, &b_b2))
       return BIO_ERR_ALIGN;
   }
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmA_tail;
   int st = A_MN ? encode_map(&tmA, a->dtype, a->a, ma, 64, kBK)
                 : encode_map(&tmA, a->dtype, a->a, ma, kBK, kBoxARows);
   if (st != BIO_OK) return st;
+  const int tail_rows = static_cast<int>(((a->m % 128) + 7) / 8 * 8);
+  if (PAIR && !A_MN && tail_rows > 0) {
+    st = encode_map(&tmA_tail, a->dtype, a->a, ma, kBK, static_cast<uint32_t>(tail_rows));
+    if (st != BIO_OK) return st;
+  } else {
+    tmA_tail = tmA;
+  }
   st = B_MN ? encode_map(&tmB, a->dtype, a->b, mb, 64, kBK)
             : encode_map(&tmB, a->dtype, a->b, mb, kBK, kBoxBRows);
   if (st != BIO_OK) return st;
@@ -982,6 +1026,25 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   p.tiles_n = static_cast<int>((a->n + BN - 1) / BN);
   p.k_blocks = static_cast<int>((a->k + kBK - 1) / kBK);
   p.group_m = group_rows(a->k, kTileM, p.tiles_m);
+  p.a_tail_rows = tail_rows;
+  p.stages = STAGES;
+  p.a_stride = 128 * kBK * 2;
+  if constexpr (PAIR) {
+    // M <= 128: no CTA ever holds a full 128-row slab, so the A stages can be
+    // packed at the tail-box stride and the freed space buys more stages.
+    if (!A_MN && a->m <= 128) {
+      using L2 = bio::Tc2Smem<BN, STAGES>;
+      const int stride = tail_rows > 0 ? tail_rows * kBK * 2 : 128 * kBK * 2;
+      int st_n = static_cast<int>(L2::kData / static_cast<uint32_t>(stride + L2::kBBytes));
+      // the last A stage is read as a full 16 KB slab: keep it inside the region
+      while (st_n > 2 && static_cast<uint32_t>((st_n - 1) * stride + 128 * kBK * 2) >
+                             static_cast<uint32_t>(st_n * (stride + L2::kBBytes)))
+        --st_n;
+      if (st_n > bio::kMaxStages2) st_n = bio::kMaxStages2;
+      p.stages = st_n;
+      p.a_stride = stride;
+    }
+  }
   p.batch2 = a->batch2;
   p.total_tiles = batch * p.tiles_m * p.tiles_n;
   p.a_div2 = static_cast<int>(a->a_div2);
@@ -1009,7 +1072,10 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   if (units <= 0) return BIO_ERR_LAUNCH;
   const int64_t n_units = p.total_tiles < units ? p.total_tiles : units;
   const int64_t grid = PAIR ? 2 * n_units : n_units;
-  kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, p);
+  if constexpr (PAIR)
+    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail, p);
+  else
+    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, p);
   return bio_host::launch_status(cudaGetLastError());
 }
 
@@ -1017,7 +1083,6 @@ template <bool A_MN, bool B_MN, typename T>
 int dispatch_bn(const bio_gemm_args* a, cudaStream_t stream) {
   const TileChoice tc = pick_tile(a->n, a->k, a->dtype);
   if (!tc.pair) return launch_tc<false, 64, A_MN, B_MN, T>(a, stream);
-  if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, stream);
   return launch_tc<true, 256, A_MN, B_MN, T>(a, stream);
 }
 
