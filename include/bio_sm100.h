@@ -44,6 +44,7 @@ extern "C" {
 #define BIO_ERR_DRIVER 6      /* driver entry point or tensor map failure    */
 #define BIO_ERR_ARG 7         /* invalid argument value (null ptr, flags)    */
 #define BIO_ERR_DEVICE 8      /* a device-side check fired (see status word) */
+#define BIO_ERR_SCRATCH 9     /* problem needs more than the fixed scratch     */
 
 /* ---- device status word bits (set by kernels, read by the host) -------- */
 #define BIO_DEV_TIMEOUT 1     /* a bounded mbarrier wait gave up             */
@@ -266,6 +267,35 @@ BIO_API int bio_moe_route_sum(int32_t dtype, const void* expert_out, int32_t w_d
                               const void* routing_weights, const int64_t* selected_experts,
                               void* out, int64_t experts, int64_t tokens, int64_t top_k,
                               int64_t hidden, int32_t device, void* stream);
+
+/* ---- convolution that allocates nothing ---------------------------------
+ * No counterpart in the reference (its convolutions allocate their im2col
+ * buffers through PyTorch on every call).  This entry point is for callers
+ * that cannot allocate device memory while they run: real-time robot control
+ * loops that reserve all memory up front (a cudaMalloc can block and
+ * synchronise the device mid-cycle), C/C++ hosts without a caching
+ * allocator, and code running inside another runtime's stream capture where
+ * allocation calls are not permitted.
+ *
+ * Same result as bio_im2col + bio_gemm (regular N-d convolution, any groups,
+ * stride, padding, dilation; bias per output channel): the patch matrix, and a
+ * zero-padded copy of the weight when its rows are not 16-byte aligned, are
+ * kept in ONE file-scope device array of BIO_NOALLOC_SCRATCH_BYTES (32 MiB)
+ * that every GPU which loads the library holds until the process exits.
+ * The caller passes contiguous x [B][C][in...], weight [O][C/G][kernel...],
+ * bias [O] or NULL and y [B][O][out...].  Problems needing more scratch
+ * (B*G*prod(out)*roundup8(C/G*prod(kernel))*dtype bytes, plus the padded
+ * weight) return BIO_ERR_SCRATCH before anything is launched.
+ * The first call on a device looks up the array's device address (module
+ * load); make that first call before any stream capture.  Every call shares
+ * the array, so calls that may overlap on the GPU (different streams, or
+ * different host threads on one device) race on it: serialise them.  Nothing
+ * in the array needs to start at zero (every byte used is written first).
+ * Never calls cudaMalloc, cudaFree or an allocating library routine. */
+#define BIO_NOALLOC_SCRATCH_BYTES (32ull << 20)
+BIO_API int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* weight,
+                                const void* bias, void* y, const bio_conv_geom* geom,
+                                int64_t out_channels, int32_t device, void* stream);
 
 #ifdef __cplusplus
 }

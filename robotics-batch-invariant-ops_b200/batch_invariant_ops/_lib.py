@@ -27,6 +27,8 @@ BIO_ERR_LAUNCH = 5
 BIO_ERR_DRIVER = 6
 BIO_ERR_ARG = 7
 BIO_ERR_DEVICE = 8
+BIO_ERR_SCRATCH = 9
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 BIO_DEV_TIMEOUT = 1
 BIO_DEV_INDEX = 2
@@ -102,6 +104,7 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_I32, _P, _I32, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     ),
+    "bio_conv_nd_noalloc": (ctypes.c_int, [_I32, _P, _P, _P, _P, _P, _I64, _I32, _P]),
     "bio_pack_rows": (
         ctypes.c_int,
         [_I32, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I32, _P],

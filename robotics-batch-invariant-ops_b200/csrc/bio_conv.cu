@@ -14,6 +14,8 @@
 // Reference: conv1d_batch_invariant (batch_invariant_ops.py:497-595, depthwise
 // kernel :435-494), conv2d_batch_invariant (:598-682), conv3d_batch_invariant
 // (:685-780), conv_transpose2d/3d_batch_invariant (:783-941).
+#include <mutex>
+
 #include "bio_common.cuh"
 
 namespace bio {
@@ -262,3 +264,111 @@ int bio_conv_transpose_scatter(int32_t dtype, const void* src, const void* bias,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Convolution without any allocation (bio_conv_nd_noalloc).
+//
+// The patch matrix (and, when needed, a packed copy of the weight) lives in a
+// fixed file-scope device array instead of caller-provided memory.  The array
+// is a host-side stand-in in host code: its device address is obtained once
+// per device with cudaGetSymbolAddress (with that device current) and passed
+// to the kernels.
+// ---------------------------------------------------------------------------
+namespace {
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[BIO_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[bio_host::kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on `device` (which must be current).
+int scratch_address(int device, unsigned char** out) {
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (g_scratch_addr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return BIO_ERR_LAUNCH;
+    g_scratch_addr[device] = p;
+  }
+  *out = static_cast<unsigned char*>(g_scratch_addr[device]);
+  return BIO_OK;
+}
+
+int64_t dtype_size(int32_t dtype) { return dtype == BIO_F32 ? 4 : 2; }
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* weight,
+                                   const void* bias, void* y, const bio_conv_geom* geom,
+                                   int64_t out_channels, int32_t device, void* stream) {
+  if (dtype != BIO_F32 && dtype != BIO_F16 && dtype != BIO_BF16) return BIO_ERR_DTYPE;
+  if (!geom_ok(geom) || out_channels < 1 || out_channels % geom->groups != 0)
+    return BIO_ERR_SHAPE;
+  const int64_t groups = geom->groups;
+  const int64_t cg = geom->channels / groups;
+  const int64_t og = out_channels / groups;
+  const int64_t kvol = geom->kernel[0] * geom->kernel[1] * geom->kernel[2];
+  const int64_t k = cg * kvol;
+  const int64_t kpad = round_up(k, 8);
+  const int64_t L = geom->out[0] * geom->out[1] * geom->out[2];
+  if (geom->batch == 0 || L == 0) return BIO_OK;
+  if (x == nullptr || weight == nullptr || y == nullptr) return BIO_ERR_ARG;
+  const int64_t es = dtype_size(dtype);
+  const int64_t patch_bytes = round_up(geom->batch * groups * L * kpad * es, 256);
+  // the tensor-core GEMM reads the weight with TMA: rows must be 16-byte
+  // aligned, otherwise a zero-padded copy goes into the scratch as well
+  const bool pack_w = dtype != BIO_F32 &&
+                      ((k * es) % 16 != 0 || (reinterpret_cast<uintptr_t>(weight) & 15u) != 0);
+  const int64_t w_bytes = pack_w ? round_up(groups * og * kpad * es, 256) : 0;
+  if (patch_bytes + w_bytes > static_cast<int64_t>(BIO_NOALLOC_SCRATCH_BYTES))
+    return BIO_ERR_SCRATCH;
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  unsigned char* scratch = nullptr;
+  st = scratch_address(device, &scratch);
+  if (st != BIO_OK) return st;
+
+  st = bio_im2col(dtype, x, geom, scratch, kpad, device, stream);
+  if (st != BIO_OK) return st;
+  const void* wa = weight;
+  int64_t w_row = k;
+  if (pack_w) {
+    st = bio_pack_rows(dtype, weight, 1, groups, og, k, 0, og * k, k, 1, scratch + patch_bytes,
+                       kpad, device, stream);
+    if (st != BIO_OK) return st;
+    wa = scratch + patch_bytes;
+    w_row = kpad;
+  }
+  bio_gemm_args g = {};
+  g.dtype = dtype;
+  g.flags = BIO_GEMM_BIAS_PER_ROW;
+  g.batch1 = geom->batch;
+  g.batch2 = groups;
+  g.m = og;
+  g.n = L;
+  g.k = k;
+  g.a = wa;
+  g.a_sm = w_row;
+  g.a_sk = 1;
+  g.a_s1 = 0;
+  g.a_s2 = og * w_row;
+  g.a_div2 = 1;
+  g.b = scratch;
+  g.b_sk = 1;
+  g.b_sn = kpad;
+  g.b_s1 = groups * L * kpad;
+  g.b_s2 = L * kpad;
+  g.b_div2 = 1;
+  g.c = y;
+  g.c_sm = L;
+  g.c_sn = 1;
+  g.c_s1 = out_channels * L;
+  g.c_s2 = og * L;
+  g.bias = bias;
+  g.bias_s2 = og;
+  g.alpha = 1.0f;
+  g.device = device;
+  return bio_gemm(&g, stream);
+}
