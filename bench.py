@@ -543,12 +543,27 @@ def run_reference(args) -> None:
 
 
 def run_profile_point(args) -> None:
-    """Minimal launch sequence for ncu captures: one GEMM point, 1 + steps launches."""
+    """Minimal launch sequence for ncu captures: one GEMM point (MxN) or one
+    attention shape (attn:B,S,causal), 1 + steps launches."""
     import torch
 
     sys.path.insert(0, str(PKG_ROOT))
-    from batch_invariant_ops import linear_batch_invariant
+    from batch_invariant_ops import linear_batch_invariant, scaled_dot_product_attention_batch_invariant
 
+    if args.profile_point.startswith("attn:"):
+        bsz, seq, causal = (int(v) for v in args.profile_point[5:].split(","))
+        dev = torch.device("cuda", 0)
+        gen = torch.Generator(device=dev).manual_seed(0)
+        q = torch.randn(bsz, 16, seq, 128, device=dev, generator=gen).to(torch.bfloat16)
+        k = torch.randn(bsz, 4, seq, 128, device=dev, generator=gen).to(torch.bfloat16)
+        v = torch.randn(bsz, 4, seq, 128, device=dev, generator=gen).to(torch.bfloat16)
+        for _ in range(1 + args.steps):
+            y = scaled_dot_product_attention_batch_invariant(q, k, v, is_causal=bool(causal),
+                                                             enable_gqa=True)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_point": args.profile_point, "launches": 1 + args.steps,
+                          "checksum": float(y.float().sum().item())}))
+        return
     m, n = (int(v) for v in args.profile_point.split("x"))
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(0)

@@ -193,12 +193,15 @@ BIO_API int bio_conv_transpose_scatter(int32_t dtype, const void* src, const voi
                                        void* stream);
 
 /* ---- attention ------------------------------------------------------------
- * Fused attention, one warp per (sequence, head, query row), keys visited in
- * fixed blocks of 32 in order with an online softmax in fp32; a row's bits do
- * not depend on the other rows, sequences or heads of the launch.  Tensors are
- * [batch][head][token][dim] through element strides (dim contiguous); KV head
- * of query head h is h / (heads / kv_heads).  Fully masked rows and empty KV
- * ranges produce zeros.  d, dv <= 256. */
+ * Fused attention with an online softmax in fp32; a row's bits do not depend
+ * on the other rows, sequences or heads of the launch.  bf16/fp16 run on
+ * tcgen05 (128 query rows per CTA, keys in fixed blocks of 128, S and O in
+ * TMEM, one softmax thread per query row); base pointers and token/head
+ * strides must then be 16-byte aligned (BIO_ERR_ALIGN otherwise).  fp32 runs
+ * on CUDA cores (one warp per query row, keys in fixed blocks of 32).  Tensors
+ * are [batch][head][token][dim] through element strides (dim contiguous); KV
+ * head of query head h is h / (heads / kv_heads).  Fully masked rows and empty
+ * KV ranges produce zeros.  d, dv <= 256. */
 #define BIO_MASK_NONE 0
 #define BIO_MASK_BOOL 1 /* uint8/bool keep-mask: 0 drops the key           */
 #define BIO_MASK_ADD 2  /* additive float mask in mask_dtype                */
@@ -232,6 +235,7 @@ typedef struct bio_attn_args {
   const void* cu_k;
   int32_t cu_is64;
   int64_t nseq;
+  void* workspace;     /* varlen, bf16/fp16: int32 [nseq + 1] scratch      */
 } bio_attn_args;
 
 /* Dense SDPA over [batch][heads][lq|lk][d|dv].  Replaces
@@ -241,8 +245,9 @@ BIO_API int bio_attention(const bio_attn_args* args, void* stream);
 /* Sequence-packed attention: q [lq tokens][heads][d], k/v [lk tokens][kv_heads]
  * (batch strides ignored); sequence s covers query tokens [cu_q[s], cu_q[s+1])
  * and keys [cu_k[s], cu_k[s+1]); query tokens outside every sequence are
- * written as zeros.  Offsets are read on the device (no host sync); invalid
- * offsets raise BIO_DEV_INDEX and zero the affected rows.  Replaces
+ * written as zeros (bf16/fp16: the caller pre-zeroes o and passes an int32
+ * [nseq + 1] workspace).  Offsets are read on the device (no host sync);
+ * invalid offsets raise BIO_DEV_INDEX and leave the affected rows zero.  Replaces
  * varlen_scaled_dot_product_attention_batch_invariant
  * (batch_invariant_ops.py:1216-1344). */
 BIO_API int bio_attention_varlen(const bio_attn_args* args, void* stream);

@@ -57,6 +57,7 @@ class _AttnArgs(ctypes.Structure):
         ("cu_k", ctypes.c_void_p),
         ("cu_is64", ctypes.c_int32),
         ("nseq", ctypes.c_int64),
+        ("workspace", ctypes.c_void_p),
     ]
 
 
@@ -67,6 +68,24 @@ MAX_HEAD_DIM = 256
 
 def _dim_contiguous(t: torch.Tensor) -> torch.Tensor:
     return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _tma_ready(t: torch.Tensor) -> torch.Tensor:
+    """[B, H, L, D] view whose non-unit strides are 16-byte multiples, with D
+    contiguous and a 16-byte aligned base (what the tensor-core kernel reads
+    with TMA).  Otherwise an exact copy with D padded to a multiple of 8; the
+    kernel still reads only the first D columns."""
+    ok = t.stride(-1) == 1 and t.data_ptr() % 16 == 0
+    for size, stride in zip(t.shape[:-1], t.stride()[:-1]):
+        if size > 1 and stride % 8 != 0:
+            ok = False
+    if ok:
+        return t
+    from . import _gemm
+
+    b, h, l, d = t.shape
+    packed, _ = _gemm._pack(t, b, h, l, d, t.stride(0), t.stride(1), t.stride(2), t.stride(3))
+    return packed
 
 
 def _check_head_dims(d: int, dv: int) -> None:
@@ -87,6 +106,8 @@ def sdpa(q, k, v, attn_mask, is_causal, scale):
     q4 = _dim_contiguous(q.reshape(nb, h, lq, d))
     k4 = _dim_contiguous(k.reshape(nb, hkv, lk, d))
     v4 = _dim_contiguous(v.reshape(nb, hkv, lk, dv))
+    if q.dtype != torch.float32:
+        q4, k4, v4 = _tma_ready(q4), _tma_ready(k4), _tma_ready(v4)
     out = torch.empty((nb, h, lq, dv), device=q.device, dtype=q.dtype)
     if out.numel() == 0:
         return out.reshape(*lead, h, lq, dv)
@@ -136,7 +157,14 @@ def varlen(q, k, v, cu_q, cu_k, *, is_causal, causal_name, scale):
     q3 = _dim_contiguous(q[0])
     k3 = _dim_contiguous(k[0])
     v3 = _dim_contiguous(v[0])
-    out = torch.empty((1, tq, h, dv), device=q.device, dtype=v.dtype)
+    half = q.dtype != torch.float32
+    if half:
+        # [T, H, D] -> [1(batch), H, T, D] views for the TMA check, back to [T, H, D]
+        q3 = _tma_ready(q3.permute(1, 0, 2).unsqueeze(0))[0].permute(1, 0, 2)
+        k3 = _tma_ready(k3.permute(1, 0, 2).unsqueeze(0))[0].permute(1, 0, 2)
+        v3 = _tma_ready(v3.permute(1, 0, 2).unsqueeze(0))[0].permute(1, 0, 2)
+    alloc = torch.zeros if half else torch.empty
+    out = alloc((1, tq, h, dv), device=q.device, dtype=v.dtype)
     if out.numel() == 0:
         return out
     cu_k = cu_k.to(cu_q.dtype) if cu_k.dtype != cu_q.dtype else cu_k
@@ -165,6 +193,10 @@ def varlen(q, k, v, cu_q, cu_k, *, is_causal, causal_name, scale):
     a.cu_q, a.cu_k = cu_q.data_ptr(), cu_k.data_ptr()
     a.cu_is64 = 1 if cu_q.dtype == torch.int64 else 0
     a.nseq = cu_q.numel() - 1
+    workspace = None
+    if half:
+        workspace = torch.empty(a.nseq + 1, dtype=torch.int32, device=q.device)
+        a.workspace = workspace.data_ptr()
     _lib.check(
         _lib.load().bio_attention_varlen(ctypes.byref(a), _lib.stream_of(q)), "bio_attention_varlen"
     )

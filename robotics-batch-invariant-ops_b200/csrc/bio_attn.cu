@@ -263,6 +263,7 @@ int run_attention(const bio_attn_args* a, bool varlen, void* stream) {
   p.mask = a->mask; p.m_sb = a->m_sb; p.m_sh = a->m_sh; p.m_sq = a->m_sq; p.m_sk = a->m_sk;
   p.cu_q = a->cu_q; p.cu_k = a->cu_k; p.cu_is64 = a->cu_is64; p.nseq = a->nseq;
   p.status = bio_host::status_word(a->device);
+  if (a->dtype != BIO_F32) return bio_host::attn_tc_launch(a, varlen, stream);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (a->dtype) {
     case BIO_F32: return dispatch_mask<float>(p, a->mask_kind, a->mask_dtype, varlen, s);

@@ -1,0 +1,715 @@
+// Tensor-core fused attention for bf16 / fp16 (dense SDPA and varlen).
+//
+// One CTA owns 128 query rows of one (sequence, head).  Keys are visited in
+// fixed blocks of 128 from the first key of the sequence:
+//   warp 0      TMA: Q tile once, then K and V tiles of each key block into a
+//               ring (128-byte swizzle; V is read N-major for the PV product).
+//   warp 1      MMA: S_j = Q K_j^T (tcgen05, M=128, N=128, fp32 in TMEM, two S
+//               buffers so S_{j+1} overlaps the softmax of block j), then
+//               O += P_j V_j (M=128, N=Dv, O accumulator resident in TMEM).
+//   warps 2..5  softmax: thread r owns query row r (its TMEM lane), reads its
+//               128 scores, applies scale and masks, keeps the running max m
+//               and sum l in fp32 (sequential over the 128 columns, so the
+//               order is fixed by the key index alone), writes P_j (rounded to
+//               the input dtype) into shared memory, rescales its O row in TMEM
+//               by exp(m_old - m_new) when the max moved, and finally stores
+//               O / l.
+// A row's arithmetic depends on its Q row, the sequence's K/V and the fixed
+// block partition only -- never on the other rows, heads or sequences of the
+// launch -- so every output row is batch invariant.  Fully masked rows and
+// empty key ranges produce zeros.  Grouped-query attention reads KV head
+// h / (H / Hkv) directly.
+//
+// Varlen: a one-thread plan kernel turns cu_seqlens_q into per-sequence
+// q-block offsets on the device; each CTA finds its (sequence, q-block) by
+// binary search, so there is no host synchronisation.  K/V rows of a partial
+// last block that belong to the next sequence are zeroed in shared memory
+// before the PV product, so neighbouring sequences cannot leak in even when
+// they hold non-finite values.
+//
+// Reference: scaled_dot_product_attention_batch_invariant
+// (batch_invariant_ops.py:1148-1213), varlen_scaled_dot_product_attention_batch_invariant
+// (:1216-1344).
+#include <mutex>
+
+#include "bio_common.cuh"
+
+namespace bio {
+
+constexpr int kAtBM = 128;
+constexpr int kAtBN = 128;
+constexpr int kAtThreads = 192;
+
+struct AttnTcParams {
+  int64_t heads, kv_heads;
+  int64_t lq, lk;  // dense lengths; varlen: packed token counts
+  int d, dv;
+  float scale;
+  int causal;
+  const void* mask;
+  int mask_kind;  // 0 none, 1 bool, 2 f32, 3 f16, 4 bf16 additive
+  int64_t m_sb, m_sh, m_sq, m_sk;
+  void* o;
+  int64_t o_sb, o_sh, o_st;
+  int varlen;
+  const void* cu_q;
+  const void* cu_k;
+  int cu_is64;
+  int64_t nseq;
+  const int* blk_start;
+  int* status;
+};
+
+template <int DP, int DVP>
+struct AttnSmem {
+  static constexpr uint32_t kQ = kAtBM * DP * 2;
+  static constexpr uint32_t kK = kAtBN * DP * 2;
+  static constexpr uint32_t kV = kAtBN * DVP * 2;
+  static constexpr uint32_t kP = kAtBM * kAtBN * 2;
+  static constexpr uint32_t kBar = 256;
+  static constexpr uint32_t kFixed = 1024 + kQ + kP + kBar;
+  static constexpr int kStages = (227u * 1024u - kFixed) / (kK + kV) >= 2 ? 2 : 1;
+  static constexpr uint32_t kTotal = kFixed + kStages * (kK + kV);
+};
+
+__device__ __forceinline__ int64_t ld_off(const void* p, int is64, int64_t i) {
+  return is64 ? static_cast<const int64_t*>(p)[i]
+              : static_cast<int64_t>(static_cast<const int*>(p)[i]);
+}
+
+__device__ __forceinline__ float mask_add(const void* m, int kind, int64_t idx) {
+  switch (kind) {
+    case 2: return static_cast<const float*>(m)[idx];
+    case 3: return __half2float(static_cast<const __half*>(m)[idx]);
+    default: return __bfloat162float(static_cast<const __nv_bfloat16*>(m)[idx]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T>
+struct AtFmt;
+template <>
+struct AtFmt<__half> {
+  static constexpr uint32_t v = 0;
+};
+template <>
+struct AtFmt<__nv_bfloat16> {
+  static constexpr uint32_t v = 1;
+};
+
+// try_wait with a suspend-time hint: a waiting warp is parked until the phase
+// completes (or the hint elapses) instead of spinning on the issue slots that
+// the softmax warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (same contract as mbar_wait) built on the sleeping try_wait.
+__device__ __forceinline__ bool at_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                        int* status) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_sleep(a, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1; i < kWaitMaxIters; ++i) {
+    if (mbar_try_wait_sleep(a, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
+  }
+  *abort_flag = 1;
+  raise_status(status, BIO_DEV_TIMEOUT);
+  return false;
+}
+
+__device__ __forceinline__ bool at_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 0; i < kWaitMaxIters; ++i) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+  return false;
+}
+
+template <int DP, int DVP, typename T>
+__global__ void __launch_bounds__(kAtThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
+  using L = AttnSmem<DP, DVP>;
+  constexpr int S = L::kStages;
+  constexpr int kQChunks = DP / 64;
+  constexpr int kVChunks = DVP / 64;
+  constexpr uint32_t kIdescS = idesc_f16(AtFmt<T>::v, kAtBM, kAtBN, false, false);
+  constexpr uint32_t kIdescO = idesc_f16(AtFmt<T>::v, kAtBM, DVP, false, true);
+  constexpr uint32_t kOCol = 256;  // TMEM: S0 [0,128), S1 [128,256), O [256, 256+DVP)
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---------------------------------------------------------------- work
+  int64_t b = 0, h = blockIdx.y, q0, lq_seq, lk_seq, q_tok0, k_tok0;
+  if (p.varlen) {
+    const int64_t g = blockIdx.x;
+    const int64_t total = p.blk_start[p.nseq];
+    if (g >= total) return;
+    int64_t lo = 0, hi = p.nseq;
+    while (hi - lo > 1) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (p.blk_start[mid] <= g) lo = mid; else hi = mid;
+    }
+    const int64_t s = lo;
+    const int64_t qs0 = ld_off(p.cu_q, p.cu_is64, s), qs1 = ld_off(p.cu_q, p.cu_is64, s + 1);
+    const int64_t ks0 = ld_off(p.cu_k, p.cu_is64, s), ks1 = ld_off(p.cu_k, p.cu_is64, s + 1);
+    const bool bad = qs0 < 0 || qs1 > p.lq || ks0 < 0 || ks1 < ks0 || ks1 > p.lk ||
+                     ld_off(p.cu_q, p.cu_is64, 0) != 0 || ld_off(p.cu_k, p.cu_is64, 0) != 0 ||
+                     (p.causal == 3 && (qs1 - qs0) != (ks1 - ks0));
+    if (bad) {
+      if (threadIdx.x == 0) raise_status(p.status, BIO_DEV_INDEX);
+      return;  // output rows stay zero (pre-zeroed by the caller)
+    }
+    q0 = (g - p.blk_start[s]) * kAtBM;
+    lq_seq = qs1 - qs0;
+    lk_seq = ks1 - ks0;
+    q_tok0 = qs0 + q0;
+    k_tok0 = ks0;
+  } else {
+    b = blockIdx.z;
+    q0 = static_cast<int64_t>(blockIdx.x) * kAtBM;
+    lq_seq = p.lq;
+    lk_seq = p.lk;
+    q_tok0 = q0;
+    k_tok0 = 0;
+  }
+  const int64_t hk = h / (p.heads / p.kv_heads);
+  const int64_t nrows = min(static_cast<int64_t>(kAtBM), lq_seq - q0);
+  const int64_t shift = (p.causal == 2) ? (lk_seq - lq_seq) : 0;
+  int64_t kend_cta = lk_seq;
+  if (p.causal != 0) kend_cta = min(lk_seq, q0 + nrows - 1 + shift + 1);
+  if (kend_cta < 0) kend_cta = 0;
+  const int nblk = static_cast<int>((kend_cta + kAtBN - 1) / kAtBN);
+
+  // per-row output pointer (softmax warps)
+  const int r = (warp & 3) * 32 + lane;
+  const int64_t i = q0 + r;
+  const bool row_valid = warp >= 2 && r < nrows;
+  T* out_row = nullptr;
+  if (row_valid) {
+    out_row = static_cast<T*>(p.o) + (p.varlen ? 0 : b * p.o_sb) + h * p.o_sh +
+              (p.varlen ? (q_tok0 + r) : i) * p.o_st;
+  }
+  if (nblk == 0) {
+    if (row_valid)
+      for (int c = 0; c < p.dv; ++c) out_row[c] = from_f32<T>(0.f);
+    return;
+  }
+
+  // ---------------------------------------------------------------- smem
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sP = sQ + L::kQ;
+  uint8_t* sK = sP + L::kP;
+  uint8_t* sV = sK + S * L::kK;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * L::kV);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;      // [S]
+  uint64_t* kv_empty = bars + 3;     // [S]
+  uint64_t* s_full = bars + 5;       // [2]
+  uint64_t* s_free = bars + 7;       // [2]
+  uint64_t* p_ready = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint64_t* mma_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 4);
+    }
+    mbar_init(p_ready, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int qc = static_cast<int>(q_tok0), kc0 = static_cast<int>(k_tok0);
+  const int hc = static_cast<int>(h), hkc = static_cast<int>(hk), bc = static_cast<int>(b);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      mbar_arrive_expect_tx(q_full, L::kQ);
+      for (int c = 0; c < kQChunks; ++c)
+        tma_load_4d(sQ + c * 16384, &tmQ, q_full, c * 64, qc, hc, bc);
+      int issued = 0;
+      for (int jb = 0; jb < nblk; ++jb) {
+        const int stage = jb % S;
+        const uint32_t ph = static_cast<uint32_t>(jb / S) & 1u;
+        if (!at_wait(&kv_empty[stage], ph ^ 1u, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&kv_full[stage], L::kK + L::kV);
+        uint8_t* k_dst = sK + stage * L::kK;
+        uint8_t* v_dst = sV + stage * L::kV;
+        const int row = kc0 + jb * kAtBN;
+        for (int c = 0; c < kQChunks; ++c)
+          tma_load_4d(k_dst + c * 16384, &tmK, &kv_full[stage], c * 64, row, hkc, bc);
+        for (int kcnk = 0; kcnk < 2; ++kcnk)
+          for (int nc = 0; nc < kVChunks; ++nc)
+            tma_load_4d(v_dst + (kcnk * kVChunks + nc) * 8192, &tmV, &kv_full[stage], nc * 64,
+                        row + kcnk * 64, hkc, bc);
+        ++issued;
+      }
+      // drain: Q and the last loads of each stage must land before exit
+      if (!at_wait_drain(q_full, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+      for (int jb = issued - 1; jb >= 0 && jb >= issued - S; --jb) {
+        if (!at_wait_drain(&kv_full[jb % S], static_cast<uint32_t>(jb / S) & 1u))
+          raise_status(p.status, BIO_DEV_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA
+      bool ok = at_wait(q_full, 0, abort_flag, p.status);
+      auto issue_s = [&](int jb) -> bool {
+        const int stage = jb % S;
+        if (!at_wait(&kv_full[stage], static_cast<uint32_t>(jb / S) & 1u, abort_flag, p.status))
+          return false;
+        const int sb = jb & 1;
+        if (!at_wait(&s_free[sb], (static_cast<uint32_t>(jb >> 1) & 1u) ^ 1u, abort_flag,
+                       p.status))
+          return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + stage * L::kK);
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16(tmem + static_cast<uint32_t>(sb * 128), smem_desc_sw128(qa + off, 16, 1024),
+                   smem_desc_sw128(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      const bool ahead = S >= 2;
+      if (ok && ahead) ok = issue_s(0);
+      for (int jb = 0; ok && jb < nblk; ++jb) {
+        if (ahead) {
+          if (jb + 1 < nblk && !issue_s(jb + 1)) break;
+        } else if (!issue_s(jb)) {
+          break;
+        }
+        if (!at_wait(p_ready, static_cast<uint32_t>(jb) & 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const int stage = jb % S;
+        const uint32_t pa = smem_u32(sP), va = smem_u32(sV + stage * L::kV);
+#pragma unroll
+        for (int kk = 0; kk < kAtBN / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t boff = (kk >> 2) * (kVChunks * 8192) + (kk & 3) * 2048;
+          umma_f16(tmem + kOCol, smem_desc_sw128(pa + aoff, 16, 1024),
+                   smem_desc_sw128(va + boff, 8192, 1024), kIdescO, (jb | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[stage]);
+        umma_commit(pv_done);
+      }
+      umma_commit(mma_done);
+      if (!at_wait_drain(mma_done, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    int64_t kr = lk_seq;  // keys visible to this row
+    if (p.causal != 0) kr = min(lk_seq, i + shift + 1);
+    if (!row_valid || kr < 0) kr = 0;
+    const int64_t mrow = (p.mask_kind != 0 && row_valid)
+                             ? b * p.m_sb + h * p.m_sh + i * p.m_sq
+                             : 0;
+    // Without masks and with a positive scale, max(s * scale) == max(s) * scale
+    // exactly (rounding is monotonic), so the hot loop runs on raw scores.
+    const bool plain = p.mask_kind == 0 && p.scale > 0.f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int jb = 0; jb < nblk; ++jb) {
+      const int sb = jb & 1;
+      const bool got = at_wait(&s_full[sb], static_cast<uint32_t>(jb >> 1) & 1u, abort_flag,
+                               p.status);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int64_t col0 = static_cast<int64_t>(jb) * kAtBN;
+      const int nvis = static_cast<int>(max(static_cast<int64_t>(0),
+                                            min(static_cast<int64_t>(kAtBN), kr - col0)));
+      const uint32_t s_addr = tmem + lane_base + static_cast<uint32_t>(sb * 128);
+      // ---- pass 1: maximum of the scaled, masked scores of this block
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), v);
+        tmem_ld_wait();
+        const int lim = nvis - c * 32;
+        if (plain) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < lim) mx = fmaxf(mx, __uint_as_float(v[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < lim) {
+              const int64_t col = col0 + c * 32 + j;
+              float sv = __uint_as_float(v[j]) * p.scale;
+              bool keep = true;
+              if (p.mask_kind == 1)
+                keep = static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] != 0;
+              else
+                sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
+              if (keep) mx = fmaxf(mx, sv);
+            }
+          }
+        }
+      }
+      if (plain && mx != -INFINITY) mx *= p.scale;
+      const float m_new = fmaxf(m, mx);
+      const float alpha = (m == -INFINITY) ? 0.f : __expf(m - m_new);
+      // ---- the P buffer and O are free once the previous PV product is done
+      if (jb > 0) {
+        const bool done = at_wait(pv_done, static_cast<uint32_t>(jb - 1) & 1u, abort_flag,
+                                  p.status);
+        if (!__all_sync(0xffffffffu, done)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, m_new != -INFINITY && alpha != 1.f)) {
+          const float a_row = (m_new != -INFINITY) ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < DVP / 32; ++c) {
+            uint32_t v[32];
+            const uint32_t ta = tmem + lane_base + kOCol + static_cast<uint32_t>(c * 32);
+            tmem_ld_32x32b_x32(ta, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * a_row);
+            tmem_st_32x32b_x32(ta, v);
+          }
+          tmem_st_wait();
+        }
+      }
+      // ---- pass 2: probabilities rounded to the input dtype, summed in column
+      // order, written straight into the 128-byte-swizzled K-major P tile
+      float lsum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), v);
+        tmem_ld_wait();
+        const int lim = nvis - c * 32;
+        float pv[32];
+        if (plain) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float pp = 0.f;
+            if (j < lim && m_new != -INFINITY)
+              pp = round_to<T>(__expf(__uint_as_float(v[j]) * p.scale - m_new));
+            pv[j] = pp;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float pp = 0.f;
+            if (j < lim && m_new != -INFINITY) {
+              const int64_t col = col0 + c * 32 + j;
+              float sv = __uint_as_float(v[j]) * p.scale;
+              bool keep = true;
+              if (p.mask_kind == 1)
+                keep = static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] != 0;
+              else
+                sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
+              if (keep && sv != -INFINITY) pp = round_to<T>(__expf(sv - m_new));
+            }
+            pv[j] = pp;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) lsum += pv[j];
+        uint8_t* base = sP + (c >> 1) * 16384 + r * 128;
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int u = (c & 1) * 4 + u4;
+          uint4 w;
+          w.x = pack_pair<T>(pv[u4 * 8 + 0], pv[u4 * 8 + 1]);
+          w.y = pack_pair<T>(pv[u4 * 8 + 2], pv[u4 * 8 + 3]);
+          w.z = pack_pair<T>(pv[u4 * 8 + 4], pv[u4 * 8 + 5]);
+          w.w = pack_pair<T>(pv[u4 * 8 + 6], pv[u4 * 8 + 7]);
+          *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) = w;
+        }
+      }
+      // S buffer may now be overwritten by the next S product
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      if (m_new != -INFINITY) {
+        l = l * alpha + lsum;
+        m = m_new;
+      }
+      // Zero V rows of a partial block that lie past the sequence end (they
+      // may belong to the next packed sequence).
+      if (p.varlen && col0 + kAtBN > lk_seq) {
+        const int stage = jb % S;
+        uint8_t* vt = sV + stage * L::kV;
+        const int first = static_cast<int>(lk_seq - col0);
+        for (int row = first + r; row < kAtBN; row += 128) {
+          const int kcnk = row >> 6, rr = row & 63;
+          for (int nc = 0; nc < kVChunks; ++nc) {
+            uint4* dst = reinterpret_cast<uint4*>(vt + (kcnk * kVChunks + nc) * 8192 + rr * 128);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) dst[u] = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+    if (ok) {
+      const bool done = at_wait(pv_done, static_cast<uint32_t>(nblk - 1) & 1u, abort_flag,
+                                p.status);
+      if (__all_sync(0xffffffffu, done)) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < DVP / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + kOCol + static_cast<uint32_t>(c * 32), v);
+          tmem_ld_wait();
+          if (row_valid) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = c * 32 + j;
+              if (col < p.dv)
+                out_row[col] = from_f32<T>(l > 0.f ? __uint_as_float(v[j]) / l : 0.f);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+__global__ void attn_plan_kernel(const void* cu_q, int is64, int64_t nseq, int* blk_start) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int acc = 0;
+  for (int64_t s = 0; s < nseq; ++s) {
+    blk_start[s] = acc;
+    const int64_t len = ld_off(cu_q, is64, s + 1) - ld_off(cu_q, is64, s);
+    if (len > 0) acc += static_cast<int>((len + kAtBM - 1) / kAtBM);
+  }
+  blk_start[nseq] = acc;
+}
+
+}  // namespace bio
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+namespace {
+
+std::mutex g_at_mu;
+
+// 4-D tensor map {dim, tokens, heads, batch} over a [batch][head][token][dim]
+// operand (element strides), 128-byte swizzle.  Size-1 dims get a harmless
+// stride.  Returns false when a stride is not TMA-expressible.
+bool at_map(CUtensorMap* map, int dtype, const void* ptr, int64_t dim, int64_t tokens,
+            int64_t heads, int64_t batch, int64_t s_tok, int64_t s_head, int64_t s_batch,
+            uint32_t box0, uint32_t box1) {
+  bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
+  if (enc == nullptr) return false;
+  const uint64_t es = 2;
+  auto fix = [&](int64_t size, int64_t stride, uint64_t prev) -> uint64_t {
+    if (size <= 1) return (prev + 15) / 16 * 16;
+    return static_cast<uint64_t>(stride) * es;
+  };
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(tokens),
+                        static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+  cuuint64_t st[3];
+  st[0] = fix(tokens, s_tok, static_cast<uint64_t>(dim) * es);
+  st[1] = fix(heads, s_head, st[0] * static_cast<uint64_t>(tokens));
+  st[2] = fix(batch, s_batch, st[1] * static_cast<uint64_t>(heads));
+  for (int i = 0; i < 3; ++i)
+    if (st[i] % 16 != 0 || st[i] == 0 || st[i] >= (1ull << 40)) return false;
+  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, 4, const_cast<void*>(ptr), dims, st, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int pad64(int v) { return v <= 64 ? 64 : (v <= 128 ? 128 : 256); }
+
+template <int DP, int DVP, typename T>
+int launch_at(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const CUtensorMap& k,
+              const CUtensorMap& v, const bio::AttnTcParams& p, cudaStream_t s) {
+  using L = bio::AttnSmem<DP, DVP>;
+  auto kern = bio::attn_tc_kernel<DP, DVP, T>;
+  static bool attr_done[bio_host::kMaxDevices] = {false};
+  {
+    std::lock_guard<std::mutex> lk(g_at_mu);
+    if (!attr_done[a->device]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+          cudaSuccess)
+        return BIO_ERR_LAUNCH;
+      attr_done[a->device] = true;
+    }
+  }
+  dim3 grid;
+  if (varlen) {
+    const int64_t g = (a->lq + bio::kAtBM - 1) / bio::kAtBM + a->nseq;
+    if (g > 2147483647) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads), 1);
+  } else {
+    const int64_t g = (a->lq + bio::kAtBM - 1) / bio::kAtBM;
+    if (g > 2147483647 || a->batch > 65535 || a->heads > 65535) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads),
+                static_cast<unsigned>(a->batch));
+  }
+  kern<<<grid, bio::kAtThreads, L::kTotal, s>>>(q, k, v, p);
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+template <typename T>
+int dispatch_at(int dp, int dvp, const bio_attn_args* a, bool varlen, const CUtensorMap& q,
+                const CUtensorMap& k, const CUtensorMap& v, const bio::AttnTcParams& p,
+                cudaStream_t s) {
+#define BIO_AT_CASE(D1, D2) \
+  if (dp == D1 && dvp == D2) return launch_at<D1, D2, T>(a, varlen, q, k, v, p, s);
+  BIO_AT_CASE(64, 64)
+  BIO_AT_CASE(64, 128)
+  BIO_AT_CASE(64, 256)
+  BIO_AT_CASE(128, 64)
+  BIO_AT_CASE(128, 128)
+  BIO_AT_CASE(128, 256)
+  BIO_AT_CASE(256, 64)
+  BIO_AT_CASE(256, 128)
+  BIO_AT_CASE(256, 256)
+#undef BIO_AT_CASE
+  return BIO_ERR_SHAPE;
+}
+
+}  // namespace
+
+namespace bio_host {
+
+int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream) {
+  if (a->dtype != BIO_BF16 && a->dtype != BIO_F16) return BIO_ERR_DTYPE;
+  if (a->d > 256 || a->dv > 256) return BIO_ERR_SHAPE;
+  if (varlen && a->workspace == nullptr) return BIO_ERR_ARG;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v)) return BIO_ERR_ALIGN;
+  const int dp = pad64(a->d), dvp = pad64(a->dv);
+  const int64_t nb = varlen ? 1 : a->batch;
+  CUtensorMap tq, tk, tv;
+  if (!at_map(&tq, a->dtype, a->q, a->d, a->lq, a->heads, nb, a->q_st, a->q_sh, a->q_sb, 64,
+              bio::kAtBM))
+    return BIO_ERR_ALIGN;
+  if (a->lk == 0) {
+    // no key at all: every row is zero and K/V are never read
+    tk = tq;
+    tv = tq;
+  } else {
+    if (!at_map(&tk, a->dtype, a->k, a->d, a->lk, a->kv_heads, nb, a->k_st, a->k_sh, a->k_sb,
+                64, bio::kAtBN))
+      return BIO_ERR_ALIGN;
+    if (!at_map(&tv, a->dtype, a->v, a->dv, a->lk, a->kv_heads, nb, a->v_st, a->v_sh, a->v_sb,
+                64, 64))
+      return BIO_ERR_ALIGN;
+  }
+  bio::AttnTcParams p;
+  p.heads = a->heads;
+  p.kv_heads = a->kv_heads;
+  p.lq = a->lq;
+  p.lk = a->lk;
+  p.d = a->d;
+  p.dv = a->dv;
+  p.scale = a->scale;
+  p.causal = a->causal;
+  p.mask = a->mask;
+  p.mask_kind = 0;
+  if (a->mask_kind == BIO_MASK_BOOL) p.mask_kind = 1;
+  if (a->mask_kind == BIO_MASK_ADD)
+    p.mask_kind = a->mask_dtype == BIO_F32 ? 2 : (a->mask_dtype == BIO_F16 ? 3 : 4);
+  p.m_sb = a->m_sb;
+  p.m_sh = a->m_sh;
+  p.m_sq = a->m_sq;
+  p.m_sk = a->m_sk;
+  p.o = a->o;
+  p.o_sb = a->o_sb;
+  p.o_sh = a->o_sh;
+  p.o_st = a->o_st;
+  p.varlen = varlen ? 1 : 0;
+  p.cu_q = a->cu_q;
+  p.cu_k = a->cu_k;
+  p.cu_is64 = a->cu_is64;
+  p.nseq = a->nseq;
+  p.blk_start = static_cast<const int*>(a->workspace);
+  p.status = bio_host::status_word(a->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (varlen) {
+    bio::attn_plan_kernel<<<1, 32, 0, s>>>(a->cu_q, a->cu_is64, a->nseq,
+                                           static_cast<int*>(a->workspace));
+    const int st = bio_host::launch_status(cudaGetLastError());
+    if (st != BIO_OK) return st;
+  }
+  if (a->dtype == BIO_BF16) return dispatch_at<__nv_bfloat16>(dp, dvp, a, varlen, tq, tk, tv, p, s);
+  return dispatch_at<__half>(dp, dvp, a, varlen, tq, tk, tv, p, s);
+}
+
+}  // namespace bio_host

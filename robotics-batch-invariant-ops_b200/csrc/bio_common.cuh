@@ -206,6 +206,25 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Store 32 lanes x 32 consecutive 32-bit columns to TMEM (inverse of
+// tmem_ld_32x32b_x32).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor for a 128-byte-swizzled tile (sm_100
 // layout: start>>4 in [0,14), LBO>>4 in [16,30), SBO>>4 in [32,46),
 // version 1 in [46,48), layout type SWIZZLE_128B (=2) in [61,64)).
@@ -333,5 +352,17 @@ int sm_count(int device);
 int* status_word(int device);
 // Map a cudaError_t to a status code (BIO_OK when success).
 int launch_status(cudaError_t e);
+
+// cuTensorMapEncodeTiled obtained through the runtime's driver entry point
+// (no link-time dependency on libcuda); nullptr when unavailable.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+// Fused tensor-core attention launch (bf16/fp16); BIO_ERR_ALIGN when the
+// operands are not expressible to TMA.
+int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream);
 
 }  // namespace bio_host

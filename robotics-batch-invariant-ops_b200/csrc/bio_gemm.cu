@@ -813,25 +813,6 @@ namespace {
 using bio::kBK;
 using bio::kBM;
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
-                                         &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
 // Operand view for a 4-D tensor map {inner, outer, level2, level1}.
 struct MapDims {
   uint64_t d[4];
@@ -883,7 +864,7 @@ bool operand_dims(uint64_t inner, uint64_t outer, int64_t outer_stride, int64_t 
 
 int encode_map(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md, uint32_t box0,
                uint32_t box1) {
-  EncodeTiledFn enc = encode_fn();
+  bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
   if (enc == nullptr) return BIO_ERR_DRIVER;
   const CUtensorMapDataType dt =
       dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

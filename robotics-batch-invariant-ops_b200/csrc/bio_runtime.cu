@@ -20,6 +20,20 @@ namespace bio_host {
 
 int launch_status(cudaError_t e) { return e == cudaSuccess ? BIO_OK : BIO_ERR_LAUNCH; }
 
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
 int ensure_device(int device) {
   if (device < 0 || device >= kMaxDevices) return BIO_ERR_ARG;
   int cur = -1;
