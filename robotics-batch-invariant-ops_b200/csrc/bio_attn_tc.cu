@@ -98,6 +98,48 @@ __device__ __forceinline__ uint32_t pack_pair<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// 2^x on the special-function unit (PTX ex2.approx).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Fixed binary trees over 32 values (the order depends only on the index).
+__device__ __forceinline__ float tree_max32(const float (&v)[32]) {
+  float t[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) t[j] = fmaxf(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) t[j] = fmaxf(t[2 * j], t[2 * j + 1]);
+  return t[0];
+}
+
+__device__ __forceinline__ float tree_sum16(float (&t)[16]) {
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) t[j] = t[2 * j] + t[2 * j + 1];
+  return t[0];
+}
+
+// Unpack a rounded pair back to fp32 (exact).
+template <typename T>
+__device__ __forceinline__ void unpack_pair(uint32_t w, float& lo, float& hi);
+template <>
+__device__ __forceinline__ void unpack_pair<__nv_bfloat16>(uint32_t w, float& lo, float& hi) {
+  lo = __uint_as_float(w << 16);
+  hi = __uint_as_float(w & 0xFFFF0000u);
+}
+template <>
+__device__ __forceinline__ void unpack_pair<__half>(uint32_t w, float& lo, float& hi) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  lo = __low2float(h);
+  hi = __high2float(h);
+}
+
 template <typename T>
 struct AtFmt;
 template <>
@@ -380,6 +422,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
                                             min(static_cast<int64_t>(kAtBN), kr - col0)));
       const uint32_t s_addr = tmem + lane_base + static_cast<uint32_t>(sb * 128);
       // ---- pass 1: maximum of the scaled, masked scores of this block
+      // (fixed tree within each 32-column chunk, chunks in order)
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -387,29 +430,31 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), v);
         tmem_ld_wait();
         const int lim = nvis - c * 32;
+        float f[32];
         if (plain) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < lim) mx = fmaxf(mx, __uint_as_float(v[j]));
+          for (int j = 0; j < 32; ++j) f[j] = (j < lim) ? __uint_as_float(v[j]) : -INFINITY;
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            float sv = -INFINITY;
             if (j < lim) {
               const int64_t col = col0 + c * 32 + j;
-              float sv = __uint_as_float(v[j]) * p.scale;
-              bool keep = true;
-              if (p.mask_kind == 1)
-                keep = static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] != 0;
-              else
+              sv = __uint_as_float(v[j]) * p.scale;
+              if (p.mask_kind == 1) {
+                if (static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] == 0) sv = -INFINITY;
+              } else {
                 sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
-              if (keep) mx = fmaxf(mx, sv);
+              }
             }
+            f[j] = sv;
           }
         }
+        mx = fmaxf(mx, tree_max32(f));
       }
       if (plain && mx != -INFINITY) mx *= p.scale;
       const float m_new = fmaxf(m, mx);
-      const float alpha = (m == -INFINITY) ? 0.f : __expf(m - m_new);
+      const float alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - m_new) * 1.4426950408889634f);
       // ---- the P buffer and O are free once the previous PV product is done
       if (jb > 0) {
         const bool done = at_wait(pv_done, static_cast<uint32_t>(jb - 1) & 1u, abort_flag,
@@ -434,8 +479,12 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           tmem_st_wait();
         }
       }
-      // ---- pass 2: probabilities rounded to the input dtype, summed in column
-      // order, written straight into the 128-byte-swizzled K-major P tile
+      // ---- pass 2: probabilities exp(s*scale - m) rounded to the input dtype,
+      // summed with a fixed tree per chunk (chunks in order), written straight
+      // into the 128-byte-swizzled K-major P tile
+      const float kLog2e = 1.4426950408889634f;
+      const float sl2 = p.scale * kLog2e;
+      const float ml2 = (m_new == -INFINITY) ? 0.f : m_new * kLog2e;
       float lsum = 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -443,44 +492,54 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), v);
         tmem_ld_wait();
         const int lim = nvis - c * 32;
-        float pv[32];
+        uint32_t w16[16];
         if (plain) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float pp = 0.f;
-            if (j < lim && m_new != -INFINITY)
-              pp = round_to<T>(__expf(__uint_as_float(v[j]) * p.scale - m_new));
-            pv[j] = pp;
+          for (int j = 0; j < 32; j += 2) {
+            const float x0 = (j < lim && m_new != -INFINITY)
+                                 ? ex2_approx(fmaf(__uint_as_float(v[j]), sl2, -ml2))
+                                 : 0.f;
+            const float x1 = (j + 1 < lim && m_new != -INFINITY)
+                                 ? ex2_approx(fmaf(__uint_as_float(v[j + 1]), sl2, -ml2))
+                                 : 0.f;
+            w16[j / 2] = pack_pair<T>(x0, x1);
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float pp = 0.f;
-            if (j < lim && m_new != -INFINITY) {
-              const int64_t col = col0 + c * 32 + j;
-              float sv = __uint_as_float(v[j]) * p.scale;
-              bool keep = true;
-              if (p.mask_kind == 1)
-                keep = static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] != 0;
-              else
-                sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
-              if (keep && sv != -INFINITY) pp = round_to<T>(__expf(sv - m_new));
+          for (int j = 0; j < 32; j += 2) {
+            float xx[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              float pp = 0.f;
+              if (j + t < lim && m_new != -INFINITY) {
+                const int64_t col = col0 + c * 32 + j + t;
+                float sv = __uint_as_float(v[j + t]) * p.scale;
+                bool keep = true;
+                if (p.mask_kind == 1)
+                  keep = static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] != 0;
+                else
+                  sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
+                if (keep && sv != -INFINITY) pp = ex2_approx((sv - m_new) * kLog2e);
+              }
+              xx[t] = pp;
             }
-            pv[j] = pp;
+            w16[j / 2] = pack_pair<T>(xx[0], xx[1]);
           }
         }
+        float t16[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) lsum += pv[j];
+        for (int j = 0; j < 16; ++j) {
+          float lo, hi;
+          unpack_pair<T>(w16[j], lo, hi);
+          t16[j] = lo + hi;
+        }
+        lsum += tree_sum16(t16);
         uint8_t* base = sP + (c >> 1) * 16384 + r * 128;
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
           const int u = (c & 1) * 4 + u4;
-          uint4 w;
-          w.x = pack_pair<T>(pv[u4 * 8 + 0], pv[u4 * 8 + 1]);
-          w.y = pack_pair<T>(pv[u4 * 8 + 2], pv[u4 * 8 + 3]);
-          w.z = pack_pair<T>(pv[u4 * 8 + 4], pv[u4 * 8 + 5]);
-          w.w = pack_pair<T>(pv[u4 * 8 + 6], pv[u4 * 8 + 7]);
-          *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) = w;
+          *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) =
+              make_uint4(w16[u4 * 4 + 0], w16[u4 * 4 + 1], w16[u4 * 4 + 2], w16[u4 * 4 + 3]);
         }
       }
       // S buffer may now be overwritten by the next S product
