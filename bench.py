@@ -209,7 +209,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     sys.path.insert(0, str(PKG_ROOT))
-    from batch_invariant_ops import _gemm, linear_batch_invariant
+    from batch_invariant_ops import _gemm, linear_batch_invariant, sharding
 
     world, rank, local = _dist()
     torch.cuda.set_device(local)
@@ -343,17 +343,12 @@ def run_ours(args) -> None:
     # identical seeds on every rank: the ranks' outputs must agree bitwise
     cross_rank_equal = None
     if world > 1:
-        y = outs[(SWEEP_M[-1], SWEEP_N[-1])].contiguous().view(torch.int16)
-        digest = torch.stack([y.to(torch.int64).sum(), (y.to(torch.int64) * 31).remainder(1000003).sum()])
-        gathered = [torch.empty_like(digest) for _ in range(world)]
-        dist.all_gather(gathered, digest)
-        cross_rank_equal = all(torch.equal(gathered[0], g) for g in gathered)
+        cross_rank_equal = sharding.ranks_agree(
+            sharding.bit_digest(outs[(SWEEP_M[-1], SWEEP_N[-1])]))
 
     # ---- max over ranks
-    t_dev = torch.tensor([dev_time, e2e_time], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t_dev, op=dist.ReduceOp.MAX)
-    dev_time, e2e_time = float(t_dev[0]), float(t_dev[1])
+    dev_time = sharding.max_over_ranks(dev_time, dev)
+    e2e_time = sharding.max_over_ranks(e2e_time, dev)
 
     if rank == 0:
         total_flops = step_flops * args.steps * world
