@@ -121,7 +121,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled tensor copies, no multicast anywhere in this library)
+// TMA (tiled tensor copies; every CTA loads its own tiles)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -251,7 +251,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t m, ui
 // ---------------------------------------------------------------------------
 // Thread-block clusters and the 2-SM (cta_group::2) tcgen05 forms.  Used by
 // the paired GEMM: both CTAs of a cluster load their halves of the operands
-// with plain (non-multicast) TMA, the leader (rank 0) issues the M=256 MMA.
+// with plain per-CTA tensor copies, the leader (rank 0) issues the M=256 MMA.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

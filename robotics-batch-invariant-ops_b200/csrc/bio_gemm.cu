@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // computes a 256 x BN tile with M=256 tcgen05.mma issued by the leader CTA.
 // CTA r loads rows [r*128, r*128+128) of the A tile and rows
 // [r*BN/2, r*BN/2 + BN/2) of the B tile into its own shared memory (plain
-// TMA, no multicast); the transaction bytes of both land on the leader's
+// per-CTA tensor copies); the transaction bytes of both land on the leader's
 // stage barrier.  Each CTA's TMEM holds its 128 output rows x BN fp32
 // columns; each CTA's epilogue stores its own rows.  Per SM this halves the
 // B bytes per flop against the single-CTA 128 x BN tile.
