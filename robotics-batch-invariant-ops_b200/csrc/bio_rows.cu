@@ -127,26 +127,98 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
         for (int j = 0; j < 8; ++j) {
           if (g * 8 + j < n) {
             if constexpr (OP == kSoftmax)
-              den += (mx == -INFINITY) ? 0.f : expf(v[j] - mx);
+              den += (mx == -INFINITY) ? 0.f : __expf(v[j] - mx);
             else
-              den += expf(v[j] - mx);
+              den += __expf(v[j] - mx);
           }
         }
       }
       den = team_reduce<TEAM, false>(den, scratch[team]);
       TO* out = y + r * n;
       if constexpr (OP == kSoftmax) {
-        const float inv_ok = den != 0.f;
+        const float inv = den != 0.f ? 1.f / den : 0.f;
         for (int64_t i = t; i < n; i += TEAM) {
           const float v = to_f32(row[i]);
-          const float e = (mx == -INFINITY) ? 0.f : expf(v - mx);
-          out[i] = from_f32<TO>(inv_ok ? e / den : 0.f);
+          const float e = (mx == -INFINITY) ? 0.f : __expf(v - mx);
+          out[i] = from_f32<TO>(e * inv);
         }
       } else {
         const float lse = logf(den);
         for (int64_t i = t; i < n; i += TEAM) {
           const float v = to_f32(row[i]);
           out[i] = from_f32<TO>(v - mx - lse);
+        }
+      }
+    }
+  }
+}
+
+// Register-resident softmax / log-softmax for rows of up to TEAM * 8 * RMAX
+// elements (RMAX groups of 8 per thread, the smallest power of two that holds
+// the row): the row is read from HBM once and written once.  The element to
+// thread assignment (8-element group g -> thread g % TEAM) and the reduction
+// tree are the same as in row_kernel, so results do not depend on which of the
+// two kernels a row length selects.
+template <typename TI, typename TO, bool LOG, int TEAM, int RMAX>
+__global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
+    row_softmax_reg_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t rows, int64_t n) {
+  constexpr int kTeamsPerBlock = TEAM >= 256 ? 1 : 256 / TEAM;
+  __shared__ float scratch[kTeamsPerBlock][TEAM / 32 + 1];
+  const int team = threadIdx.x / TEAM;
+  const int t = threadIdx.x % TEAM;
+  const int64_t groups = (n + 7) / 8;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTeamsPerBlock + team; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * kTeamsPerBlock) {
+    const TI* row = x + r * n;
+    float v[RMAX][8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q) {
+      const int64_t g = t + static_cast<int64_t>(q) * TEAM;
+      if (g < groups) {
+        load_group(row, g, n, v[q], -INFINITY);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[q][j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q][j] = -INFINITY;
+      }
+    }
+    mx = team_reduce<TEAM, true>(mx, scratch[team]);
+    float den = 0.f;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q) {
+      const int64_t g = t + static_cast<int64_t>(q) * TEAM;
+      if (g < groups) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (g * 8 + j < n) {
+            float e;
+            if (LOG)
+              e = __expf(v[q][j] - mx);
+            else
+              e = (mx == -INFINITY) ? 0.f : __expf(v[q][j] - mx);
+            den += e;
+            if (!LOG) v[q][j] = e;
+          }
+        }
+      }
+    }
+    den = team_reduce<TEAM, false>(den, scratch[team]);
+    TO* out = y + r * n;
+    const float lse = LOG ? logf(den) : 0.f;
+    const float inv = den != 0.f ? 1.f / den : 0.f;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q) {
+      const int64_t g = t + static_cast<int64_t>(q) * TEAM;
+      if (g < groups) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int64_t idx = g * 8 + j;
+          if (idx < n) {
+            const float o = LOG ? (v[q][j] - mx - lse) : v[q][j] * inv;
+            out[idx] = from_f32<TO>(o);
+          }
         }
       }
     }
@@ -177,20 +249,98 @@ __global__ void __launch_bounds__(256)
       for (int64_t j = 0; j < n; ++j) {
         const float v = to_f32(base[j * inner]);
         if constexpr (OP == kSoftmax)
-          den += (mx == -INFINITY) ? 0.f : expf(v - mx);
+          den += (mx == -INFINITY) ? 0.f : __expf(v - mx);
         else
-          den += expf(v - mx);
+          den += __expf(v - mx);
       }
       TO* out = y + o * n * inner + i;
       if constexpr (OP == kSoftmax) {
+        const float inv = den != 0.f ? 1.f / den : 0.f;
         for (int64_t j = 0; j < n; ++j) {
           const float v = to_f32(base[j * inner]);
-          const float e = (mx == -INFINITY) ? 0.f : expf(v - mx);
-          out[j * inner] = from_f32<TO>(den != 0.f ? e / den : 0.f);
+          const float e = (mx == -INFINITY) ? 0.f : __expf(v - mx);
+          out[j * inner] = from_f32<TO>(e * inv);
         }
       } else {
         const float lse = logf(den);
         for (int64_t j = 0; j < n; ++j) out[j * inner] = from_f32<TO>(to_f32(base[j * inner]) - mx - lse);
+      }
+    }
+  }
+}
+
+
+// Column mode, vectorised: one thread owns 8 adjacent columns (16-byte loads
+// for 2-byte types) and keeps 8 independent running values, each folded over
+// n in increasing order exactly as col_kernel folds a single column.
+template <typename TI, typename TO, int OP>
+__global__ void __launch_bounds__(256)
+    col_kernel_vec8(const TI* __restrict__ x, TO* __restrict__ y, int64_t outer, int64_t n,
+                    int64_t inner) {
+  static_assert(sizeof(TI) == 2, "vector path is for 2-byte inputs");
+  const int64_t vecs = outer * (inner / 8);
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < vecs;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = c / (inner / 8), i0 = (c - o * (inner / 8)) * 8;
+    const TI* base = x + o * n * inner + i0;
+    float acc[8];
+    if constexpr (OP == kMean || OP == kL2Norm) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+      for (int64_t j = 0; j < n; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
+        const TI* e = reinterpret_cast<const TI*>(&w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float v = to_f32(e[k]);
+          acc[k] += (OP == kL2Norm) ? v * v : v;
+        }
+      }
+      TO* out = y + o * inner + i0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        out[k] = from_f32<TO>((OP == kMean) ? acc[k] / static_cast<float>(n) : sqrtf(acc[k]));
+    } else {
+      float mx[8], den[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        mx[k] = -INFINITY;
+        den[k] = 0.f;
+      }
+      for (int64_t j = 0; j < n; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
+        const TI* e = reinterpret_cast<const TI*>(&w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], to_f32(e[k]));
+      }
+      for (int64_t j = 0; j < n; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
+        const TI* e = reinterpret_cast<const TI*>(&w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float v = to_f32(e[k]);
+          if constexpr (OP == kSoftmax)
+            den[k] += (mx[k] == -INFINITY) ? 0.f : __expf(v - mx[k]);
+          else
+            den[k] += __expf(v - mx[k]);
+        }
+      }
+      TO* out = y + o * n * inner + i0;
+      for (int64_t j = 0; j < n; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
+        const TI* e = reinterpret_cast<const TI*>(&w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float v = to_f32(e[k]);
+          float r;
+          if constexpr (OP == kSoftmax) {
+            const float inv = den[k] != 0.f ? 1.f / den[k] : 0.f;
+            r = ((mx[k] == -INFINITY) ? 0.f : __expf(v - mx[k])) * inv;
+          } else {
+            r = v - mx[k] - logf(den[k]);
+          }
+          out[j * inner + k] = from_f32<TO>(r);
+        }
       }
     }
   }
@@ -216,15 +366,45 @@ int launch_rows(const void* x, void* y, int64_t outer, int64_t n, int64_t inner,
     const int team = team_for(n);
     const int64_t per_block = team >= 256 ? 1 : 256 / team;
     int64_t blocks = (outer + per_block - 1) / per_block;
-    const int64_t cap = static_cast<int64_t>(sms) * 32;
+    const int64_t cap = static_cast<int64_t>(sms) * 64;
     if (blocks > cap) blocks = cap;
     const unsigned g = static_cast<unsigned>(blocks);
+    if ((OP == bio::kSoftmax || OP == bio::kLogSoftmax) && team <= 256 && n <= team * 64) {
+      constexpr bool kLog = OP == bio::kLogSoftmax;
+      const int64_t per = (n + 8 * team - 1) / (8 * team);  // groups per thread
+      const int rmax = per <= 1 ? 1 : (per <= 2 ? 2 : (per <= 4 ? 4 : 8));
+#define BIO_REG_CASE(TM, R)                                                                  \
+  if (team == TM && rmax == R) {                                                             \
+    bio::row_softmax_reg_kernel<TI, TO, kLog, TM, R><<<g, 256, 0, stream>>>(xi, yo, outer, n); \
+    return bio_host::launch_status(cudaGetLastError());                                      \
+  }
+      BIO_REG_CASE(32, 1)
+      BIO_REG_CASE(32, 2)
+      BIO_REG_CASE(32, 4)
+      BIO_REG_CASE(32, 8)
+      BIO_REG_CASE(256, 1)
+      BIO_REG_CASE(256, 2)
+      BIO_REG_CASE(256, 4)
+      BIO_REG_CASE(256, 8)
+#undef BIO_REG_CASE
+    }
     switch (team) {
       case 32: bio::row_kernel<TI, TO, OP, 32><<<g, 256, 0, stream>>>(xi, yo, outer, n); break;
       case 256: bio::row_kernel<TI, TO, OP, 256><<<g, 256, 0, stream>>>(xi, yo, outer, n); break;
       default: bio::row_kernel<TI, TO, OP, 1024><<<g, 1024, 0, stream>>>(xi, yo, outer, n); break;
     }
   } else {
+    if constexpr (sizeof(TI) == 2) {
+      if (inner % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        const int64_t vecs = outer * (inner / 8);
+        int64_t blocks = (vecs + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(sms) * 64;
+        if (blocks > cap) blocks = cap;
+        bio::col_kernel_vec8<TI, TO, OP><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            xi, yo, outer, n, inner);
+        return bio_host::launch_status(cudaGetLastError());
+      }
+    }
     const int64_t cols = outer * inner;
     int64_t blocks = (cols + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sms) * 64;

@@ -437,3 +437,17 @@ def test_moe_out_of_range_expert_sets_status_not_trap():
     assert _lib.device_status() & _lib.BIO_DEV_INDEX
     assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[0]) > 0
     _lib.clear_device_status()
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_column_mode_vectorised_reductions(dtype):
+    """Reductions over a non-last dim with inner % 8 == 0 (8 columns per thread)."""
+    gen = torch.Generator(device="cuda").manual_seed(7080)
+    x = _rn(3, 40, 4, 48, dtype=dtype, gen=gen)  # dim 1 reduced, inner = 192
+    _close_to_oracle(softmax(x, 1), O.softmax(x, 1), dtype)
+    _close_to_oracle(log_softmax(x, 1), O.log_softmax(x, 1), dtype)
+    _close_to_oracle(mean_dim(x, 1), O.mean(x, (1,)), dtype)
+    _close_to_oracle(linalg_vector_norm_batch_invariant(x, dim=1), O.vector_norm(x, (1,)), dtype)
+    assert torch.equal(softmax(x[:1], 1), softmax(x, 1)[:1])
+    assert torch.equal(linalg_vector_norm_batch_invariant(x[:1], dim=1),
+                       linalg_vector_norm_batch_invariant(x, dim=1)[:1])
