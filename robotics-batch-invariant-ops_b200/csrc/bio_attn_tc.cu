@@ -38,7 +38,7 @@ namespace bio {
 
 constexpr int kAtBM = 128;
 constexpr int kAtBN = 128;
-constexpr int kAtThreads = 192;
+constexpr int kAtMaxThreads = 320;  // TMA, MMA, up to 8 softmax warps (2 per TMEM lane quarter)
 
 struct AttnTcParams {
   int64_t heads, kv_heads;
@@ -60,6 +60,9 @@ struct AttnTcParams {
   int* status;
 };
 
+// Shared memory plan.  HALVES = 2 splits every query row between two softmax
+// warps (64 score columns each) that exchange partial max / sum through kX;
+// the largest head sizes (256/256) keep one warp per row to fit 227 KB.
 template <int DP, int DVP>
 struct AttnSmem {
   static constexpr uint32_t kQ = kAtBM * DP * 2;
@@ -67,9 +70,12 @@ struct AttnSmem {
   static constexpr uint32_t kV = kAtBN * DVP * 2;
   static constexpr uint32_t kP = kAtBM * kAtBN * 2;
   static constexpr uint32_t kBar = 256;
-  static constexpr uint32_t kFixed = 1024 + kQ + kP + kBar;
+  static constexpr int kHalves = (DP == 256 && DVP == 256) ? 1 : 2;
+  static constexpr uint32_t kX = kHalves == 2 ? 2 * 2 * 128 * 4 : 0;
+  static constexpr uint32_t kFixed = 1024 + kQ + kP + kBar + kX;
   static constexpr int kStages = (227u * 1024u - kFixed) / (kK + kV) >= 2 ? 2 : 1;
   static constexpr uint32_t kTotal = kFixed + kStages * (kK + kV);
+  static constexpr int kThreads = 64 + 128 * kHalves;
 };
 
 __device__ __forceinline__ int64_t ld_off(const void* p, int is64, int64_t i) {
@@ -193,11 +199,13 @@ __device__ __forceinline__ bool at_wait_drain(uint64_t* bar, uint32_t parity) {
 }
 
 template <int DP, int DVP, typename T>
-__global__ void __launch_bounds__(kAtThreads, 1)
+__global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
   using L = AttnSmem<DP, DVP>;
   constexpr int S = L::kStages;
+  constexpr int HALVES = L::kHalves;
+  constexpr int CPT = 4 / HALVES;  // 32-column score chunks per softmax thread
   constexpr int kQChunks = DP / 64;
   constexpr int kVChunks = DVP / 64;
   constexpr uint32_t kIdescS = idesc_f16(AtFmt<T>::v, kAtBM, kAtBN, false, false);
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               (p.varlen ? (q_tok0 + r) : i) * p.o_st;
   }
   if (nblk == 0) {
-    if (row_valid)
+    if (row_valid && warp < 6)
       for (int c = 0; c < p.dv; ++c) out_row[c] = from_f32<T>(0.f);
     return;
   }
@@ -281,8 +289,11 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   uint64_t* p_ready = bars + 9;
   uint64_t* pv_done = bars + 10;
   uint64_t* mma_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* xbar = bars + 12;        // [4] pair exchange, one per TMEM lane quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xmax = reinterpret_cast<float*>(sV + S * L::kV + L::kBar);  // [2][128]
+  float* xsum = xmax + 256;                                          // [2][128]
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -292,9 +303,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 4);
+      mbar_init(&s_free[s], 4 * HALVES);
     }
-    mbar_init(p_ready, 4);
+    mbar_init(p_ready, 4 * HALVES);
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 64);
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -396,7 +408,12 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- softmax
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    // Warp w >= 2 owns TMEM lane quarter (w & 3) = 32 query rows, and score
+    // columns [half*64*CPT/2 ...) of every block when a row is split in halves.
+    const int half = (warp - 2) >> 2;  // 0 or 1 (always 0 when HALVES == 1)
+    const int qtr = warp & 3;
+    const int st = (warp - 2) * 32 + lane;  // softmax thread index 0 .. 128*HALVES-1
+    const uint32_t lane_base = static_cast<uint32_t>(qtr * 32) << 16;
     int64_t kr = lk_seq;  // keys visible to this row
     if (p.causal != 0) kr = min(lk_seq, i + shift + 1);
     if (!row_valid || kr < 0) kr = 0;
@@ -406,6 +423,26 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     // Without masks and with a positive scale, max(s * scale) == max(s) * scale
     // exactly (rounding is monotonic), so the hot loop runs on raw scores.
     const bool plain = p.mask_kind == 0 && p.scale > 0.f;
+    const float kLog2e = 1.4426950408889634f;
+    const float sl2 = p.scale * kLog2e;
+    uint32_t xround = 0;
+    // Exchange one float per row with the partner warp of the same quarter;
+    // both receive (v_half0, v_half1).  Bounded like every other wait.
+    auto exchange = [&](float* buf, float mine, float& v0, float& v1) -> bool {
+      if constexpr (HALVES == 1) {
+        v0 = mine;
+        v1 = 0.f;
+        return true;
+      } else {
+        buf[half * 128 + r] = mine;
+        mbar_arrive(&xbar[qtr]);
+        const bool okx = at_wait(&xbar[qtr], xround & 1u, abort_flag, p.status);
+        ++xround;
+        v0 = buf[r];
+        v1 = buf[128 + r];
+        return okx;
+      }
+    };
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int jb = 0; jb < nblk; ++jb) {
@@ -425,11 +462,12 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       // (fixed tree within each 32-column chunk, chunks in order)
       float mx = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < CPT; ++c) {
+        const int ca = half * CPT + c;
         uint32_t v[32];
-        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), v);
+        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(ca * 32), v);
         tmem_ld_wait();
-        const int lim = nvis - c * 32;
+        const int lim = nvis - ca * 32;
         float f[32];
         if (plain) {
 #pragma unroll
@@ -439,7 +477,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           for (int j = 0; j < 32; ++j) {
             float sv = -INFINITY;
             if (j < lim) {
-              const int64_t col = col0 + c * 32 + j;
+              const int64_t col = col0 + ca * 32 + j;
               sv = __uint_as_float(v[j]) * p.scale;
               if (p.mask_kind == 1) {
                 if (static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] == 0) sv = -INFINITY;
@@ -452,9 +490,18 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         mx = fmaxf(mx, tree_max32(f));
       }
+      {
+        float x0, x1;
+        const bool okx = exchange(xmax, mx, x0, x1);
+        if (!__all_sync(0xffffffffu, okx)) {
+          ok = false;
+          break;
+        }
+        mx = (HALVES == 2) ? fmaxf(x0, x1) : x0;
+      }
       if (plain && mx != -INFINITY) mx *= p.scale;
       const float m_new = fmaxf(m, mx);
-      const float alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - m_new) * 1.4426950408889634f);
+      const float alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - m_new) * kLog2e);
       // ---- the P buffer and O are free once the previous PV product is done
       if (jb > 0) {
         const bool done = at_wait(pv_done, static_cast<uint32_t>(jb - 1) & 1u, abort_flag,
@@ -467,7 +514,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         if (__any_sync(0xffffffffu, m_new != -INFINITY && alpha != 1.f)) {
           const float a_row = (m_new != -INFINITY) ? alpha : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < DVP / 32; ++c) {
+          for (int c = half * (DVP / 32 / HALVES); c < (half + 1) * (DVP / 32 / HALVES); ++c) {
             uint32_t v[32];
             const uint32_t ta = tmem + lane_base + kOCol + static_cast<uint32_t>(c * 32);
             tmem_ld_32x32b_x32(ta, v);
@@ -480,18 +527,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
       }
       // ---- pass 2: probabilities exp(s*scale - m) rounded to the input dtype,
-      // summed with a fixed tree per chunk (chunks in order), written straight
-      // into the 128-byte-swizzled K-major P tile
-      const float kLog2e = 1.4426950408889634f;
-      const float sl2 = p.scale * kLog2e;
+      // summed with a fixed tree per chunk (chunks in order, then half 0 + half
+      // 1), written straight into the 128-byte-swizzled K-major P tile
       const float ml2 = (m_new == -INFINITY) ? 0.f : m_new * kLog2e;
       float lsum = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < CPT; ++c) {
+        const int ca = half * CPT + c;
         uint32_t v[32];
-        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), v);
+        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(ca * 32), v);
         tmem_ld_wait();
-        const int lim = nvis - c * 32;
+        const int lim = nvis - ca * 32;
         uint32_t w16[16];
         if (plain) {
 #pragma unroll
@@ -512,7 +558,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             for (int t = 0; t < 2; ++t) {
               float pp = 0.f;
               if (j + t < lim && m_new != -INFINITY) {
-                const int64_t col = col0 + c * 32 + j + t;
+                const int64_t col = col0 + ca * 32 + j + t;
                 float sv = __uint_as_float(v[j + t]) * p.scale;
                 bool keep = true;
                 if (p.mask_kind == 1)
@@ -534,10 +580,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           t16[j] = lo + hi;
         }
         lsum += tree_sum16(t16);
-        uint8_t* base = sP + (c >> 1) * 16384 + r * 128;
+        uint8_t* base = sP + (ca >> 1) * 16384 + r * 128;
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
-          const int u = (c & 1) * 4 + u4;
+          const int u = (ca & 1) * 4 + u4;
           *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) =
               make_uint4(w16[u4 * 4 + 0], w16[u4 * 4 + 1], w16[u4 * 4 + 2], w16[u4 * 4 + 3]);
         }
@@ -546,6 +592,15 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
+      {
+        float x0, x1;
+        const bool okx = exchange(xsum, lsum, x0, x1);
+        if (!__all_sync(0xffffffffu, okx)) {
+          ok = false;
+          break;
+        }
+        lsum = (HALVES == 2) ? x0 + x1 : x0;
+      }
       if (m_new != -INFINITY) {
         l = l * alpha + lsum;
         m = m_new;
@@ -556,7 +611,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         const int stage = jb % S;
         uint8_t* vt = sV + stage * L::kV;
         const int first = static_cast<int>(lk_seq - col0);
-        for (int row = first + r; row < kAtBN; row += 128) {
+        for (int row = first + st; row < kAtBN; row += 128 * HALVES) {
           const int kcnk = row >> 6, rr = row & 63;
           for (int nc = 0; nc < kVChunks; ++nc) {
             uint4* dst = reinterpret_cast<uint4*>(vt + (kcnk * kVChunks + nc) * 8192 + rr * 128);
@@ -576,7 +631,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < DVP / 32; ++c) {
+        for (int c = half * (DVP / 32 / HALVES); c < (half + 1) * (DVP / 32 / HALVES); ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem + lane_base + kOCol + static_cast<uint32_t>(c * 32), v);
           tmem_ld_wait();
@@ -680,7 +735,7 @@ int launch_at(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const C
     grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads),
                 static_cast<unsigned>(a->batch));
   }
-  kern<<<grid, bio::kAtThreads, L::kTotal, s>>>(q, k, v, p);
+  kern<<<grid, L::kThreads, L::kTotal, s>>>(q, k, v, p);
   return bio_host::launch_status(cudaGetLastError());
 }
 
