@@ -424,7 +424,6 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
     // exactly (rounding is monotonic), so the hot loop runs on raw scores.
     const bool plain = p.mask_kind == 0 && p.scale > 0.f;
     const float kLog2e = 1.4426950408889634f;
-    const float sl2 = p.scale * kLog2e;
     uint32_t xround = 0;
     // Exchange one float per row with the partner warp of the same quarter;
     // both receive (v_half0, v_half1).  Bounded like every other wait.
@@ -458,20 +457,22 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
       const int nvis = static_cast<int>(max(static_cast<int64_t>(0),
                                             min(static_cast<int64_t>(kAtBN), kr - col0)));
       const uint32_t s_addr = tmem + lane_base + static_cast<uint32_t>(sb * 128);
-      // ---- pass 1: maximum of the scaled, masked scores of this block
-      // (fixed tree within each 32-column chunk, chunks in order)
+      // ---- pass 1: this thread's CPT chunks of 32 scores stay in registers;
+      // maximum of the scaled, masked scores (fixed tree within each chunk,
+      // chunks in order, then half 0 vs half 1)
+      float f[CPT][32];
       float mx = -INFINITY;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < CPT; ++c) {
         const int ca = half * CPT + c;
         uint32_t v[32];
         tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(ca * 32), v);
         tmem_ld_wait();
         const int lim = nvis - ca * 32;
-        float f[32];
         if (plain) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = (j < lim) ? __uint_as_float(v[j]) : -INFINITY;
+          for (int j = 0; j < 32; ++j)
+            f[c][j] = (j < lim) ? __uint_as_float(v[j]) * p.scale : -INFINITY;
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -485,11 +486,15 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
                 sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
               }
             }
-            f[j] = sv;
+            f[c][j] = sv;
           }
         }
-        mx = fmaxf(mx, tree_max32(f));
+        mx = fmaxf(mx, tree_max32(f[c]));
       }
+      // S buffer may now be overwritten by the next S product
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
       {
         float x0, x1;
         const bool okx = exchange(xmax, mx, x0, x1);
@@ -499,9 +504,13 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
         }
         mx = (HALVES == 2) ? fmaxf(x0, x1) : x0;
       }
-      if (plain && mx != -INFINITY) mx *= p.scale;
-      const float m_new = fmaxf(m, mx);
-      const float alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - m_new) * kLog2e);
+      // Reference point of the exponentials: the running max m moves only when
+      // the block max exceeds it by more than 8 (log2 units), so P stays
+      // <= 2^8 and the O rescale round trip through TMEM is rare.  The choice
+      // depends on this row's own scores only.
+      const bool move = (m == -INFINITY) ? (mx != -INFINITY) : (mx > m + 8.f / kLog2e);
+      const float m_new = move ? mx : m;
+      const float alpha = (m == -INFINITY || !move) ? 1.f : ex2_approx((m - m_new) * kLog2e);
       // ---- the P buffer and O are free once the previous PV product is done
       if (jb > 0) {
         const bool done = at_wait(pv_done, static_cast<uint32_t>(jb - 1) & 1u, abort_flag,
@@ -511,8 +520,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, m_new != -INFINITY && alpha != 1.f)) {
-          const float a_row = (m_new != -INFINITY) ? alpha : 1.f;
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
           for (int c = half * (DVP / 32 / HALVES); c < (half + 1) * (DVP / 32 / HALVES); ++c) {
             uint32_t v[32];
@@ -520,7 +528,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
             tmem_ld_32x32b_x32(ta, v);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * a_row);
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
             tmem_st_32x32b_x32(ta, v);
           }
           tmem_st_wait();
@@ -531,46 +539,16 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
       // 1), written straight into the 128-byte-swizzled K-major P tile
       const float ml2 = (m_new == -INFINITY) ? 0.f : m_new * kLog2e;
       float lsum = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < CPT; ++c) {
         const int ca = half * CPT + c;
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(ca * 32), v);
-        tmem_ld_wait();
-        const int lim = nvis - ca * 32;
         uint32_t w16[16];
-        if (plain) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const float x0 = (j < lim && m_new != -INFINITY)
-                                 ? ex2_approx(fmaf(__uint_as_float(v[j]), sl2, -ml2))
-                                 : 0.f;
-            const float x1 = (j + 1 < lim && m_new != -INFINITY)
-                                 ? ex2_approx(fmaf(__uint_as_float(v[j + 1]), sl2, -ml2))
-                                 : 0.f;
-            w16[j / 2] = pack_pair<T>(x0, x1);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float xx[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              float pp = 0.f;
-              if (j + t < lim && m_new != -INFINITY) {
-                const int64_t col = col0 + ca * 32 + j + t;
-                float sv = __uint_as_float(v[j + t]) * p.scale;
-                bool keep = true;
-                if (p.mask_kind == 1)
-                  keep = static_cast<const uint8_t*>(p.mask)[mrow + col * p.m_sk] != 0;
-                else
-                  sv += mask_add(p.mask, p.mask_kind, mrow + col * p.m_sk);
-                if (keep && sv != -INFINITY) pp = ex2_approx((sv - m_new) * kLog2e);
-              }
-              xx[t] = pp;
-            }
-            w16[j / 2] = pack_pair<T>(xx[0], xx[1]);
-          }
+        for (int j = 0; j < 32; j += 2) {
+          const float s0 = f[c][j], s1 = f[c][j + 1];
+          const float x0 = (s0 != -INFINITY) ? ex2_approx(fmaf(s0, kLog2e, -ml2)) : 0.f;
+          const float x1 = (s1 != -INFINITY) ? ex2_approx(fmaf(s1, kLog2e, -ml2)) : 0.f;
+          w16[j / 2] = pack_pair<T>(x0, x1);
         }
         float t16[16];
 #pragma unroll
@@ -588,10 +566,6 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
               make_uint4(w16[u4 * 4 + 0], w16[u4 * 4 + 1], w16[u4 * 4 + 2], w16[u4 * 4 + 3]);
         }
       }
-      // S buffer may now be overwritten by the next S product
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
       {
         float x0, x1;
         const bool okx = exchange(xsum, lsum, x0, x1);
