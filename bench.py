@@ -550,6 +550,173 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# per-operator table (--ops): every operator family of the path on a
+# representative BASELINE shape, ours vs stock PyTorch vs the reference's
+# Triton implementation, with algorithmic flops / bytes and roofline fractions
+# ---------------------------------------------------------------------------
+def _ops_cases(api, dev):
+    """[(name, fn, flops, bytes, stock_fn)] built against the module ``api``
+    (this package or the reference package: same public names)."""
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rn(*shape, dtype=torch.bfloat16, scale=1.0):
+        return (torch.randn(*shape, device=dev, generator=g) * scale).to(dtype)
+
+    cases = []
+    # GEMM (config 2 extremes)
+    x1, x8k = rn(1, 4096), rn(8192, 4096)
+    w, b = rn(16384, 4096, scale=1 / 64), rn(16384, scale=0.02)
+    cases.append(("linear M=1 N=16384 K=4096 bf16", lambda: api.linear_batch_invariant(x1, w, b),
+                  2 * 16384 * 4096, 2 * (4096 + 16384 * 4096 + 16384 + 16384),
+                  lambda: F.linear(x1, w, b)))
+    cases.append(("linear M=8192 N=16384 K=4096 bf16", lambda: api.linear_batch_invariant(x8k, w, b),
+                  2 * 8192 * 16384 * 4096, 2 * (8192 * 4096 + 16384 * 4096 + 8192 * 16384),
+                  lambda: F.linear(x8k, w, b)))
+    # fp32 mm (config 1)
+    a32 = torch.linspace(-100, 100, 2048 * 4096, device=dev).reshape(2048, 4096)
+    w32 = torch.linspace(-100, 100, 4096 * 4096, device=dev).reshape(4096, 4096)
+    cases.append(("mm fp32 2048x4096x4096 (config 1)", lambda: api.matmul_persistent(a32, w32),
+                  2 * 2048 * 4096 * 4096, 4 * (2 * 2048 * 4096 + 4096 * 4096),
+                  lambda: torch.mm(a32, w32)))
+    # attention (config 3)
+    for bsz, seq, causal in ((4, 4096, True), (16, 1024, False)):
+        q = rn(bsz, 16, seq, 128)
+        k, v = rn(bsz, 4, seq, 128), rn(bsz, 4, seq, 128)
+        fl = 4 * bsz * 16 * seq * seq * 128 // (2 if causal else 1)
+        by = 2 * (2 * bsz * 16 * seq * 128 + 2 * bsz * 4 * seq * 128)
+        cases.append((f"sdpa B={bsz} S={seq} H16/4 D128 {'causal' if causal else 'full'} bf16",
+                      lambda q=q, k=k, v=v, c=causal: api.scaled_dot_product_attention_batch_invariant(
+                          q, k, v, is_causal=c, enable_gqa=True),
+                      fl, by,
+                      lambda q=q, k=k, v=v, c=causal: F.scaled_dot_product_attention(
+                          q, k, v, is_causal=c, enable_gqa=True)))
+    q = rn(2, 16, 1024, 128)
+    k, v = rn(2, 4, 1024, 128), rn(2, 4, 1024, 128)
+    keep = torch.rand(2, 1, 1024, 1024, device=dev, generator=g) > 0.1
+    cases.append(("sdpa B=2 S=1024 bool mask p=0.1 bf16",
+                  lambda: api.scaled_dot_product_attention_batch_invariant(q, k, v, attn_mask=keep,
+                                                                          enable_gqa=True),
+                  4 * 2 * 16 * 1024 * 1024 * 128, 2 * (2 * 2 * 16 * 1024 * 128 + 2 * 2 * 4 * 1024 * 128)
+                  + 2 * 1024 * 1024,
+                  lambda: F.scaled_dot_product_attention(q, k, v, attn_mask=keep, enable_gqa=True)))
+    lens = torch.randint(16, 2049, (32,), generator=torch.Generator().manual_seed(0)).tolist()
+    cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), device=dev,
+                      dtype=torch.int32)
+    tot = int(cu[-1])
+    vq, vk, vv = rn(1, tot, 16, 128), rn(1, tot, 4, 128), rn(1, tot, 4, 128)
+    vfl = sum(4 * 16 * L * (L + 1) // 2 * 128 for L in lens)
+    cases.append(("varlen 32 seqs U[16,2048] H16/4 D128 top-left causal bf16",
+                  lambda: api.varlen_scaled_dot_product_attention_batch_invariant(
+                      vq, vk, vv, cu, cu, is_causal=True, causal_type="TopLeft"),
+                  vfl, 2 * tot * (16 + 4 + 4 + 16) * 128, None))
+    # MoE (config 4)
+    hid = rn(1024, 2048)
+    gw, uw = rn(8, 5632, 2048, scale=0.02), rn(8, 5632, 2048, scale=0.02)
+    dw = rn(8, 2048, 5632, scale=0.02)
+    logits = torch.randn(1024, 8, device=dev, generator=g)
+    top, sel = torch.topk(logits, 2)
+    rw = torch.softmax(top, -1)
+    cases.append(("moe T=1024 E=8 top-2 2048->5632 bf16 (dense, as the reference)",
+                  lambda: api.deterministic_token_choice_moe(hid, rw, sel, gw, uw, dw),
+                  6 * 1024 * 8 * 2048 * 5632, 2 * 3 * 8 * 2048 * 5632, None))
+    # convolutions
+    img = rn(32, 3, 224, 224)
+    pw = rn(1152, 3, 14, 14, scale=0.02)
+    cases.append(("conv2d SigLIP patch14 B=32 bf16",
+                  lambda: api.conv2d_batch_invariant(img, pw, None, (14, 14), (0, 0), (1, 1), False,
+                                                     (0, 0), 1),
+                  2 * 32 * 256 * 1152 * 588, 2 * (img.numel() + pw.numel() + 32 * 1152 * 256),
+                  lambda: F.conv2d(img, pw, stride=14)))
+    sig = rn(8, 6144, 650)
+    dwk = rn(6144, 1, 4)
+    cases.append(("conv1d depthwise [8,6144,650] k4 p3 bf16",
+                  lambda: api.conv1d_batch_invariant(sig, dwk, None, (1,), (3,), (1,), False, (0,), 6144),
+                  2 * 8 * 6144 * 653 * 4, 2 * (sig.numel() + 8 * 6144 * 653),
+                  lambda: F.conv1d(sig, dwk, padding=3, groups=6144)))
+    lat = rn(8, 256, 24, 24)
+    tw = rn(256, 256, 4, 4, scale=0.05)
+    cases.append(("conv_transpose2d [8,256,24,24] 4x4 s4 bf16",
+                  lambda: api.conv_transpose2d_batch_invariant(lat, tw, None, (4, 4), (0, 0), (1, 1),
+                                                               (0, 0), 1),
+                  2 * 8 * 576 * 256 * 4096, 2 * (lat.numel() + tw.numel() + 8 * 256 * 96 * 96),
+                  lambda: F.conv_transpose2d(lat, tw, stride=4)))
+    # row kernels
+    sc = rn(65536, 4096)
+    cases.append(("softmax [65536,4096] bf16", lambda: api.softmax(sc, -1), 0, 4 * sc.numel(),
+                  lambda: torch.softmax(sc, -1)))
+    lm = rn(64, 257152)
+    cases.append(("log_softmax [64,257152] bf16", lambda: api.log_softmax(lm, -1), 0, 4 * lm.numel(),
+                  lambda: torch.log_softmax(lm, -1)))
+    hs = rn(4096, 2048)
+    cases.append(("mean dim -1 [4096,2048] bf16", lambda: api.mean_dim(hs, -1), 0,
+                  2 * hs.numel() + 2 * 4096, lambda: hs.mean(-1)))
+    vol = rn(8, 1024, 4, 132, 160)
+    cases.append(("vector_norm dim 1 [8,1024,4,132,160] bf16",
+                  lambda: api.linalg_vector_norm_batch_invariant(vol, dim=1), 0,
+                  2 * vol.numel() + 2 * vol.numel() // 1024,
+                  lambda: torch.linalg.vector_norm(vol, dim=1)))
+    return cases
+
+
+def _time_op(fn, flush, reps=5):
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e-3)
+    return statistics.median(times)
+
+
+def run_ops(args) -> None:
+    import torch
+
+    dev = torch.device("cuda", 0)
+    if args.ops_reference:
+        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+        import batch_invariant_ops as api
+
+        assert "baseline" in api.__file__
+    else:
+        sys.path.insert(0, str(PKG_ROOT))
+        import batch_invariant_ops as api
+    flush = _Flusher(dev)
+    peaks, _ = _peaks()
+    rows = []
+    for name, fn, fl, by, stock in _ops_cases(api, dev):
+        try:
+            t = _time_op(fn, flush)
+        except Exception as exc:  # the reference may not support a case
+            rows.append({"op": name, "error": f"{type(exc).__name__}: {str(exc)[:120]}"})
+            continue
+        row = {"op": name, "us": round(t * 1e6, 1)}
+        if fl:
+            row["tflops"] = round(fl / t / 1e12, 1)
+        row["gbs"] = round(by / t / 1e9, 1)
+        ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+        if fl and fl / by >= ridge:
+            row["bound"], row["frac"] = "tensor", round(fl / t / 1e12 / peaks["bf16_tflops"], 3)
+        else:
+            row["bound"], row["frac"] = "hbm", round(by / t / 1e9 / peaks["hbm_gbs"], 3)
+        if stock is not None and not args.ops_reference:
+            row["stock_us"] = round(_time_op(stock, flush) * 1e6, 1)
+        rows.append(row)
+        del fn
+    print(json.dumps({"impl": "reference-triton" if args.ops_reference else "ours", "ops": rows}),
+          flush=True)
+
+
 def run_profile_point(args) -> None:
     """Minimal launch sequence for ncu captures: one GEMM point (MxN) or one
     attention shape (attn:B,S,causal), 1 + steps launches."""
@@ -596,8 +763,13 @@ def main() -> None:
     parser.add_argument("--no-triton-ref", action="store_true")
     parser.add_argument("--triton-ref-worker", action="store_true", help=argparse.SUPPRESS)
     parser.add_argument("--profile-point", default=None, help="MxN: run one GEMM point (for ncu)")
+    parser.add_argument("--ops", action="store_true", help="per-operator roofline table")
+    parser.add_argument("--ops-reference", action="store_true",
+                        help="with --ops: time the reference package from baseline/_ref")
     args = parser.parse_args()
-    if args.profile_point:
+    if args.ops:
+        run_ops(args)
+    elif args.profile_point:
         run_profile_point(args)
     elif args.triton_ref_worker:
         run_triton_ref_worker(args)

@@ -116,6 +116,18 @@ BIO_API int bio_gemm(const bio_gemm_args* args, void* stream);
  * block_m * 1000000 + block_n * 1000 + block_k. */
 BIO_API int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype);
 
+/* bio_gemm with an explicit output tile for the tensor-core path (f16/bf16):
+ * tile_m 128 (one CTA) or 256 (CTA pair), tile_n 32/64/128/256 (pair: 128 or
+ * 256; an N-contiguous B needs tile_n >= 64).  The per-element arithmetic of
+ * every tile is the same sequence (64-wide K blocks in increasing order, four
+ * K=16 MMAs per block into an fp32 accumulator, one rounding), so all tiles
+ * must produce identical bits; tests use this entry to check exactly that.
+ * BIO_ERR_ARG for an unsupported tile.  No counterpart in the reference
+ * (its matmul_persistent, batch_invariant_ops.py:271-343, has one fixed
+ * configuration per dtype). */
+BIO_API int bio_gemm_tiled(const bio_gemm_args* args, int32_t tile_m, int32_t tile_n,
+                           void* stream);
+
 /* Copy a strided [nb1][nb2][rows][cols] operand into a dense
  * [nb1][nb2][rows][cols_pad] buffer (cols_pad >= cols, zero filled tail).
  * Used to bring odd strides into the 16-byte aligned K-contiguous layout the

@@ -189,8 +189,10 @@ def launch(
     bias_per_row: bool = False,
     bias_s2: int = 0,
     alpha: float = 1.0,
+    tile: tuple[int, int] | None = None,
 ) -> None:
-    """Enqueue one bio_gemm on the current stream of ``c``'s device."""
+    """Enqueue one bio_gemm on the current stream of ``c``'s device (with
+    ``tile`` = (tile_m, tile_n): bio_gemm_tiled, an explicit output tile)."""
     args = _lib.GemmArgs()
     args.dtype = _lib.DTYPE_CODE[c.dtype]
     args.flags = _lib.BIO_GEMM_BIAS_PER_ROW if bias_per_row else 0
@@ -219,11 +221,23 @@ def launch(
     args.bias_s2 = bias_s2
     args.alpha = alpha
     args.device = c.device.index
-    _lib.check(_lib.load().bio_gemm(ctypes.byref(args), _lib.stream_of(c)), "bio_gemm")
+    if tile is None:
+        _lib.check(_lib.load().bio_gemm(ctypes.byref(args), _lib.stream_of(c)), "bio_gemm")
+    else:
+        _lib.check(
+            _lib.load().bio_gemm_tiled(ctypes.byref(args), tile[0], tile[1], _lib.stream_of(c)),
+            "bio_gemm_tiled",
+        )
 
 
-def mm(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """C[M,N] = A[M,K] @ B[K,N] (+ bias[N]); any strides."""
+def mm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    tile: tuple[int, int] | None = None,
+) -> torch.Tensor:
+    """C[M,N] = A[M,K] @ B[K,N] (+ bias[N]); any strides.  ``tile`` forces an
+    output tile (tests of tile independence)."""
     m, k = a.shape
     n = b.shape[1]
     c = torch.empty((m, n), device=a.device, dtype=a.dtype)
@@ -237,7 +251,8 @@ def mm(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None) -> to
         opa = operand_a(a, 1, 1, m, k, a.stride(0), a.stride(1), 0, 0)
         opb = operand_b(b, 1, 1, k, n, b.stride(0), b.stride(1), 0, 0)
     launch(
-        opa, opb, c, batch1=1, batch2=1, m=m, n=n, k=k, c_sm=n, c_sn=1, c_s1=0, c_s2=0, bias=bias
+        opa, opb, c, batch1=1, batch2=1, m=m, n=n, k=k, c_sm=n, c_sn=1, c_s1=0, c_s2=0, bias=bias,
+        tile=tile,
     )
     return c
 

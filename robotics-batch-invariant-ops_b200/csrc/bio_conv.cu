@@ -25,97 +25,131 @@ struct Geom {
   int64_t in[3], kernel[3], stride[3], padding[3], dilation[3], out[3];
 };
 
+// One warp per patch row (b, group, l): the row's output position and input
+// base are decomposed once, lanes walk the row's kpad entries (32-bit index
+// arithmetic within the row) and store them contiguously.
 template <typename T>
-__global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ patches, Geom g,
-                              int64_t k_real, int64_t kpad, int64_t total) {
-  const int64_t kvol = g.kernel[0] * g.kernel[1] * g.kernel[2];
+__global__ void __launch_bounds__(256)
+    im2col_kernel(const T* __restrict__ x, T* __restrict__ patches, Geom g, int64_t k_real,
+                  int64_t kpad, int64_t rows) {
+  const uint32_t k1 = static_cast<uint32_t>(g.kernel[1]);
+  const uint32_t k2 = static_cast<uint32_t>(g.kernel[2]);
+  const uint32_t kvol = static_cast<uint32_t>(g.kernel[0]) * k1 * k2;
   const int64_t L = g.out[0] * g.out[1] * g.out[2];
   const int64_t cg = g.channels / g.groups;
   const int64_t in_vol = g.in[0] * g.in[1] * g.in[2];
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t kk = idx % kpad;
-    int64_t rest = idx / kpad;
-    const int64_t l = rest % L;
-    rest /= L;
-    const int64_t grp = rest % g.groups;
-    const int64_t b = rest / g.groups;
-    T v = from_f32<T>(0.f);
-    if (kk < k_real) {
-      const int64_t c = kk / kvol;
-      int64_t z = kk - c * kvol;
-      const int64_t z2 = z % g.kernel[2];
-      z /= g.kernel[2];
-      const int64_t z1 = z % g.kernel[1];
-      const int64_t z0 = z / g.kernel[1];
-      const int64_t o2 = l % g.out[2];
-      const int64_t t = l / g.out[2];
-      const int64_t o1 = t % g.out[1];
-      const int64_t o0 = t / g.out[1];
-      const int64_t i0 = o0 * g.stride[0] - g.padding[0] + z0 * g.dilation[0];
-      const int64_t i1 = o1 * g.stride[1] - g.padding[1] + z1 * g.dilation[1];
-      const int64_t i2 = o2 * g.stride[2] - g.padding[2] + z2 * g.dilation[2];
-      if (i0 >= 0 && i0 < g.in[0] && i1 >= 0 && i1 < g.in[1] && i2 >= 0 && i2 < g.in[2]) {
-        const int64_t ch = grp * cg + c;
-        v = x[(b * g.channels + ch) * in_vol + (i0 * g.in[1] + i1) * g.in[2] + i2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+       row < rows; row += warps) {
+    const int64_t l = row % L;
+    const int64_t bg = row / L;
+    const int64_t grp = bg % g.groups;
+    const int64_t b = bg / g.groups;
+    const int64_t o2 = l % g.out[2];
+    const int64_t t = l / g.out[2];
+    const int64_t o1 = t % g.out[1];
+    const int64_t o0 = t / g.out[1];
+    const int64_t b0 = o0 * g.stride[0] - g.padding[0];
+    const int64_t b1 = o1 * g.stride[1] - g.padding[1];
+    const int64_t b2 = o2 * g.stride[2] - g.padding[2];
+    const T* xs = x + (b * g.channels + grp * cg) * in_vol;
+    T* dst = patches + row * kpad;
+    for (int64_t kk = lane; kk < kpad; kk += 32) {
+      T v = from_f32<T>(0.f);
+      if (kk < k_real) {
+        const uint32_t k32 = static_cast<uint32_t>(kk);
+        const uint32_t c = k32 / kvol;
+        uint32_t z = k32 - c * kvol;
+        const uint32_t z12 = z % (k1 * k2);
+        const uint32_t z0 = z / (k1 * k2);
+        const uint32_t z1 = z12 / k2;
+        const uint32_t z2 = z12 - z1 * k2;
+        const int64_t i0 = b0 + static_cast<int64_t>(z0) * g.dilation[0];
+        const int64_t i1 = b1 + static_cast<int64_t>(z1) * g.dilation[1];
+        const int64_t i2 = b2 + static_cast<int64_t>(z2) * g.dilation[2];
+        if (i0 >= 0 && i0 < g.in[0] && i1 >= 0 && i1 < g.in[1] && i2 >= 0 && i2 < g.in[2])
+          v = xs[static_cast<int64_t>(c) * in_vol + (i0 * g.in[1] + i1) * g.in[2] + i2];
       }
+      dst[kk] = v;
     }
-    patches[idx] = v;
   }
 }
 
+// One warp per (sample, channel) row; lanes walk the output positions, each
+// folding its taps in order k = 0..K-1 in fp32, bias added after the taps.
 template <typename T>
-__global__ void depthwise_conv1d_kernel(const T* __restrict__ x, const T* __restrict__ w,
-                                        const T* __restrict__ bias, T* __restrict__ y,
-                                        int64_t channels, int64_t lin, int64_t lout, int ksize,
-                                        int stride, int pad, int dil, int64_t total) {
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t l = idx % lout;
-    const int64_t bc = idx / lout;
+__global__ void __launch_bounds__(256)
+    depthwise_conv1d_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                            const T* __restrict__ bias, T* __restrict__ y, int64_t channels,
+                            int64_t lin, int64_t lout, int ksize, int stride, int pad, int dil,
+                            int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t bc = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+       bc < rows; bc += warps) {
     const int64_t c = bc % channels;
     const T* xr = x + bc * lin;
     const T* wr = w + c * ksize;
-    float acc = 0.f;
-    for (int k = 0; k < ksize; ++k) {
-      const int64_t i = l * stride - pad + static_cast<int64_t>(k) * dil;
-      if (i >= 0 && i < lin) acc += to_f32(xr[i]) * to_f32(wr[k]);
+    const float bv = bias != nullptr ? to_f32(bias[c]) : 0.f;
+    T* yr = y + bc * lout;
+    for (int64_t l = lane; l < lout; l += 32) {
+      float acc = 0.f;
+      const int64_t i0 = l * stride - pad;
+      for (int k = 0; k < ksize; ++k) {
+        const int64_t i = i0 + static_cast<int64_t>(k) * dil;
+        if (i >= 0 && i < lin) acc += to_f32(xr[i]) * to_f32(wr[k]);
+      }
+      if (bias != nullptr) acc += bv;
+      yr[l] = from_f32<T>(acc);
     }
-    if (bias != nullptr) acc += to_f32(bias[c]);
-    y[idx] = from_f32<T>(acc);
   }
 }
 
-// dst[b, g*Og + o, s*k + z ...] = src[b, g, o*kvol + z, s] (+ bias[g*Og + o])
+// dst[b, g*Og + o, s*k + z ...] = src[b, g, o*kvol + z, s] (+ bias[g*Og + o]).
+// One warp per output row (b, oc, p0, p1) of length D2 = s2*k2: lane X reads
+// src[..., z2 = X % k2][i2 = X / k2] and the row is written contiguously; the
+// (i2, z2) pair advances by 32 positions per step without a division.
 template <typename T>
-__global__ void convt_scatter_kernel(const T* __restrict__ src, const T* __restrict__ bias,
-                                     T* __restrict__ dst, Geom g, int64_t og, int64_t total) {
+__global__ void __launch_bounds__(256)
+    convt_scatter_kernel(const T* __restrict__ src, const T* __restrict__ bias,
+                         T* __restrict__ dst, Geom g, int64_t og, int64_t rows) {
   const int64_t k0 = g.kernel[0], k1 = g.kernel[1], k2 = g.kernel[2];
-  const int64_t s0 = g.in[0], s1 = g.in[1], s2 = g.in[2];
-  const int64_t d1 = s1 * k1, d2 = s2 * k2;
-  const int64_t out_vol = s0 * k0 * d1 * d2;
-  const int64_t in_vol = s0 * s1 * s2;
+  const int64_t s1 = g.in[1], s2 = g.in[2];
+  const int64_t d0 = g.in[0] * k0, d1 = s1 * k1, d2 = s2 * k2;
+  const int64_t in_vol = g.in[0] * s1 * s2;
   const int64_t kvol = k0 * k1 * k2;
   const int64_t cout = og * g.groups;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    int64_t pos = idx % out_vol;
-    const int64_t bc = idx / out_vol;
-    const int64_t oc = bc % cout;
-    const int64_t b = bc / cout;
-    const int64_t p2 = pos % d2;
-    pos /= d2;
-    const int64_t p1 = pos % d1;
-    const int64_t p0 = pos / d1;
+  const int lane = threadIdx.x & 31;
+  const int64_t step_i = 32 / k2, step_z = 32 % k2;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+       r < rows; r += warps) {
+    const int64_t p1 = r % d1;
+    int64_t rest = r / d1;
+    const int64_t p0 = rest % d0;
+    rest /= d0;
+    const int64_t oc = rest % cout;
+    const int64_t b = rest / cout;
     const int64_t i0 = p0 / k0, z0 = p0 - i0 * k0;
     const int64_t i1 = p1 / k1, z1 = p1 - i1 * k1;
-    const int64_t i2 = p2 / k2, z2 = p2 - i2 * k2;
     const int64_t grp = oc / og, o = oc - grp * og;
-    const int64_t q = o * kvol + (z0 * k1 + z1) * k2 + z2;
-    const int64_t i = (i0 * s1 + i1) * s2 + i2;
-    float v = to_f32(src[((b * g.groups + grp) * og * kvol + q) * in_vol + i]);
-    if (bias != nullptr) v += to_f32(bias[oc]);
-    dst[idx] = from_f32<T>(v);
+    const T* srow = src + ((b * g.groups + grp) * og * kvol + o * kvol + (z0 * k1 + z1) * k2) * in_vol +
+                    (i0 * s1 + i1) * s2;
+    const float bv = bias != nullptr ? to_f32(bias[oc]) : 0.f;
+    T* drow = dst + r * d2;
+    int64_t i2 = lane / k2, z2 = lane - (lane / k2) * k2;
+    for (int64_t X = lane; X < d2; X += 32) {
+      float v = to_f32(srow[z2 * in_vol + i2]);
+      if (bias != nullptr) v += bv;
+      drow[X] = from_f32<T>(v);
+      i2 += step_i;
+      z2 += step_z;
+      if (z2 >= k2) {
+        z2 -= k2;
+        ++i2;
+      }
+    }
   }
 }
 
@@ -139,8 +173,9 @@ bio::Geom to_geom(const bio_conv_geom* c) {
   return g;
 }
 
-unsigned blocks_for(int64_t total) {
-  int64_t b = (total + 255) / 256;
+// Grid for the warp-per-row kernels (8 warps per 256-thread block).
+unsigned blocks_for_rows(int64_t rows) {
+  int64_t b = (rows + 7) / 8;
   if (b > 65536 * 4) b = 65536 * 4;
   return static_cast<unsigned>(b);
 }
@@ -173,19 +208,20 @@ int bio_im2col(int32_t dtype, const void* x, const bio_conv_geom* geom, void* pa
   if (st != BIO_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bio::Geom g = to_geom(geom);
+  const int64_t rows = geom->batch * geom->groups * L;
   switch (dtype) {
     case BIO_F32:
-      bio::im2col_kernel<float><<<blocks_for(total), 256, 0, s>>>(
-          static_cast<const float*>(x), static_cast<float*>(patches), g, k_real, kpad, total);
+      bio::im2col_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(
+          static_cast<const float*>(x), static_cast<float*>(patches), g, k_real, kpad, rows);
       break;
     case BIO_F16:
-      bio::im2col_kernel<__half><<<blocks_for(total), 256, 0, s>>>(
-          static_cast<const __half*>(x), static_cast<__half*>(patches), g, k_real, kpad, total);
+      bio::im2col_kernel<__half><<<blocks_for_rows(rows), 256, 0, s>>>(
+          static_cast<const __half*>(x), static_cast<__half*>(patches), g, k_real, kpad, rows);
       break;
     case BIO_BF16:
-      bio::im2col_kernel<__nv_bfloat16><<<blocks_for(total), 256, 0, s>>>(
+      bio::im2col_kernel<__nv_bfloat16><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(patches), g, k_real,
-          kpad, total);
+          kpad, rows);
       break;
     default: return BIO_ERR_DTYPE;
   }
@@ -205,24 +241,25 @@ int bio_depthwise_conv1d(int32_t dtype, const void* x, const void* w, const void
   int st = bio_host::ensure_device(device);
   if (st != BIO_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t rows = batch * channels;
   switch (dtype) {
     case BIO_F32:
-      bio::depthwise_conv1d_kernel<float><<<blocks_for(total), 256, 0, s>>>(
+      bio::depthwise_conv1d_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const float*>(x), static_cast<const float*>(w),
           static_cast<const float*>(bias), static_cast<float*>(y), channels, lin, lout, ksize,
-          stride, padding, dilation, total);
+          stride, padding, dilation, rows);
       break;
     case BIO_F16:
-      bio::depthwise_conv1d_kernel<__half><<<blocks_for(total), 256, 0, s>>>(
+      bio::depthwise_conv1d_kernel<__half><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const __half*>(x), static_cast<const __half*>(w),
           static_cast<const __half*>(bias), static_cast<__half*>(y), channels, lin, lout, ksize,
-          stride, padding, dilation, total);
+          stride, padding, dilation, rows);
       break;
     case BIO_BF16:
-      bio::depthwise_conv1d_kernel<__nv_bfloat16><<<blocks_for(total), 256, 0, s>>>(
+      bio::depthwise_conv1d_kernel<__nv_bfloat16><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
           static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y), channels, lin,
-          lout, ksize, stride, padding, dilation, total);
+          lout, ksize, stride, padding, dilation, rows);
       break;
     default: return BIO_ERR_DTYPE;
   }
@@ -242,21 +279,22 @@ int bio_conv_transpose_scatter(int32_t dtype, const void* src, const void* bias,
   if (st != BIO_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bio::Geom g = to_geom(geom);
+  const int64_t rows = total / (geom->in[2] * geom->kernel[2]);
   switch (dtype) {
     case BIO_F32:
-      bio::convt_scatter_kernel<float><<<blocks_for(total), 256, 0, s>>>(
+      bio::convt_scatter_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const float*>(src), static_cast<const float*>(bias),
-          static_cast<float*>(dst), g, out_channels_per_group, total);
+          static_cast<float*>(dst), g, out_channels_per_group, rows);
       break;
     case BIO_F16:
-      bio::convt_scatter_kernel<__half><<<blocks_for(total), 256, 0, s>>>(
+      bio::convt_scatter_kernel<__half><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const __half*>(src), static_cast<const __half*>(bias),
-          static_cast<__half*>(dst), g, out_channels_per_group, total);
+          static_cast<__half*>(dst), g, out_channels_per_group, rows);
       break;
     case BIO_BF16:
-      bio::convt_scatter_kernel<__nv_bfloat16><<<blocks_for(total), 256, 0, s>>>(
+      bio::convt_scatter_kernel<__nv_bfloat16><<<blocks_for_rows(rows), 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(src), static_cast<const __nv_bfloat16*>(bias),
-          static_cast<__nv_bfloat16*>(dst), g, out_channels_per_group, total);
+          static_cast<__nv_bfloat16*>(dst), g, out_channels_per_group, rows);
       break;
     default: return BIO_ERR_DTYPE;
   }

@@ -898,7 +898,7 @@ TileChoice pick_tile(int64_t n, int64_t /*k*/, int32_t /*dtype*/) {
 template <bool PAIR, int BN>
 constexpr int stages_for() {
   if (PAIR) return BN == 128 ? 8 : 6;
-  return BN == 64 ? 8 : (BN == 128 ? 6 : 4);
+  return BN <= 64 ? 8 : (BN == 128 ? 6 : 4);
 }
 
 std::mutex g_attr_mu;
@@ -1060,19 +1060,35 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   return bio_host::launch_status(cudaGetLastError());
 }
 
+// Tile configurations compiled into the library: (pair, bn).
+bool tile_supported(const TileChoice& tc) {
+  if (tc.pair) return tc.bn == 128 || tc.bn == 256;
+  return tc.bn == 32 || tc.bn == 64 || tc.bn == 128 || tc.bn == 256;
+}
+
 template <bool A_MN, bool B_MN, typename T>
-int dispatch_bn(const bio_gemm_args* a, cudaStream_t stream) {
-  const TileChoice tc = pick_tile(a->n, a->k, a->dtype);
-  if (!tc.pair) return launch_tc<false, 64, A_MN, B_MN, T>(a, stream);
-  return launch_tc<true, 256, A_MN, B_MN, T>(a, stream);
+int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream) {
+  if (tc.pair) {
+    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, stream);
+    return launch_tc<true, 256, A_MN, B_MN, T>(a, stream);
+  }
+  switch (tc.bn) {
+    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, stream);
+    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, stream);
+    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, stream);
+    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, stream);
+  }
 }
 
 template <typename T>
-int dispatch_tc(const bio_gemm_args* a, cudaStream_t stream, bool a_mn, bool b_mn) {
+int dispatch_tc(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream, bool a_mn,
+                bool b_mn) {
   if (a_mn) {
-    return b_mn ? dispatch_bn<true, true, T>(a, stream) : dispatch_bn<true, false, T>(a, stream);
+    return b_mn ? dispatch_bn<true, true, T>(a, tc, stream)
+                : dispatch_bn<true, false, T>(a, tc, stream);
   }
-  return b_mn ? dispatch_bn<false, true, T>(a, stream) : dispatch_bn<false, false, T>(a, stream);
+  return b_mn ? dispatch_bn<false, true, T>(a, tc, stream)
+              : dispatch_bn<false, false, T>(a, tc, stream);
 }
 
 int launch_f32(const bio_gemm_args* a, cudaStream_t stream) {
@@ -1137,7 +1153,13 @@ int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype) {
   return (tc.pair ? 256 : kBM) * 1000000 + tc.bn * 1000 + kBK;
 }
 
-int bio_gemm(const bio_gemm_args* a, void* stream_v) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of bio_gemm / bio_gemm_tiled; `forced` (when non-null) replaces
+// the library's tile choice for the tensor-core path.
+int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v) {
   if (a == nullptr) return BIO_ERR_ARG;
   if ((a->flags & ~BIO_GEMM_BIAS_PER_ROW) != 0) return BIO_ERR_ARG;
   if (a->m < 0 || a->n < 0 || a->k < 0 || a->batch1 < 0 || a->batch2 < 1) return BIO_ERR_SHAPE;
@@ -1181,8 +1203,29 @@ int bio_gemm(const bio_gemm_args* a, void* stream_v) {
   } else {
     return BIO_ERR_STRIDE;
   }
-  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, stream, a_mn, b_mn);
-  return dispatch_tc<__half>(a, stream, a_mn, b_mn);
+  TileChoice tc = forced != nullptr ? *forced : pick_tile(a->n, a->k, a->dtype);
+  if (!tile_supported(tc)) return BIO_ERR_ARG;
+  // An N-contiguous B is staged in 64-column swizzle atoms: tiles narrower
+  // than one atom are not built for it.
+  if (b_mn && !tc.pair && tc.bn < 64) {
+    if (forced != nullptr) return BIO_ERR_ARG;
+    tc.bn = 64;
+  }
+  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn);
+  return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bio_gemm(const bio_gemm_args* a, void* stream_v) { return gemm_impl(a, nullptr, stream_v); }
+
+int bio_gemm_tiled(const bio_gemm_args* a, int32_t tile_m, int32_t tile_n, void* stream_v) {
+  if (tile_m != 128 && tile_m != 256) return BIO_ERR_ARG;
+  const TileChoice tc{tile_m == 256, static_cast<int>(tile_n)};
+  if (!tile_supported(tc)) return BIO_ERR_ARG;
+  return gemm_impl(a, &tc, stream_v);
 }
 
 int bio_pack_rows(int32_t dtype, const void* src, int64_t nb1, int64_t nb2, int64_t rows,

@@ -48,6 +48,36 @@ __device__ __forceinline__ void load_group(const T* __restrict__ row, int64_t g,
   }
 }
 
+// Store 8 consecutive outputs of group g: one 16-byte store (two for fp32)
+// when the group is complete and aligned, element stores otherwise.
+template <typename TO>
+__device__ __forceinline__ void store_group(TO* __restrict__ row, int64_t g, int64_t n,
+                                            const float (&o)[8]) {
+  const int64_t base = g * 8;
+  TO* p = row + base;
+  if (base + 8 <= n && (reinterpret_cast<uintptr_t>(p) % 16) == 0) {
+    if constexpr (sizeof(TO) == 2) {
+      uint4 w;
+      TO* e = reinterpret_cast<TO*>(&w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[j] = from_f32<TO>(o[j]);
+      *reinterpret_cast<uint4*>(p) = w;
+    } else {
+      *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<float4*>(p + 4) = make_float4(o[4], o[5], o[6], o[7]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (base + j < n) p[j] = from_f32<TO>(o[j]);
+  }
+}
+
+// Loads of kUnroll groups are issued before any of them is folded, so that
+// several 16-byte loads per thread are in flight; the fold order (increasing
+// g, elements in order) is unchanged.
+constexpr int kUnroll = 4;
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -99,11 +129,17 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
     const TI* row = x + r * n;
     if constexpr (OP == kMean || OP == kL2Norm) {
       float acc = 0.f;
-      for (int64_t g = t; g < groups; g += TEAM) {
-        float v[8];
-        load_group(row, g, n, v, 0.f);
+      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
+        float v[kUnroll][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc += (OP == kL2Norm) ? v[j] * v[j] : v[j];
+        for (int u = 0; u < kUnroll; ++u)
+          if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], 0.f);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (g0 + u * TEAM < groups) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += (OP == kL2Norm) ? v[u][j] * v[u][j] : v[u][j];
+          }
       }
       const float s = team_reduce<TEAM, false>(acc, scratch[team]);
       if (t == 0) {
@@ -112,41 +148,64 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
       }
     } else {
       float mx = -INFINITY;
-      for (int64_t g = t; g < groups; g += TEAM) {
-        float v[8];
-        load_group(row, g, n, v, -INFINITY);
+      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
+        float v[kUnroll][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[j]);
+        for (int u = 0; u < kUnroll; ++u)
+          if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], -INFINITY);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (g0 + u * TEAM < groups) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[u][j]);
+          }
       }
       mx = team_reduce<TEAM, true>(mx, scratch[team]);
       float den = 0.f;
-      for (int64_t g = t; g < groups; g += TEAM) {
-        float v[8];
-        load_group(row, g, n, v, -INFINITY);
+      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
+        float v[kUnroll][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (g * 8 + j < n) {
-            if constexpr (OP == kSoftmax)
-              den += (mx == -INFINITY) ? 0.f : __expf(v[j] - mx);
-            else
-              den += __expf(v[j] - mx);
+        for (int u = 0; u < kUnroll; ++u)
+          if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], -INFINITY);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t g = g0 + u * TEAM;
+          if (g < groups) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (g * 8 + j < n) {
+                if constexpr (OP == kSoftmax)
+                  den += (mx == -INFINITY) ? 0.f : __expf(v[u][j] - mx);
+                else
+                  den += __expf(v[u][j] - mx);
+              }
+            }
           }
         }
       }
       den = team_reduce<TEAM, false>(den, scratch[team]);
       TO* out = y + r * n;
-      if constexpr (OP == kSoftmax) {
-        const float inv = den != 0.f ? 1.f / den : 0.f;
-        for (int64_t i = t; i < n; i += TEAM) {
-          const float v = to_f32(row[i]);
-          const float e = (mx == -INFINITY) ? 0.f : __expf(v - mx);
-          out[i] = from_f32<TO>(e * inv);
-        }
-      } else {
-        const float lse = logf(den);
-        for (int64_t i = t; i < n; i += TEAM) {
-          const float v = to_f32(row[i]);
-          out[i] = from_f32<TO>(v - mx - lse);
+      const float inv = den != 0.f ? 1.f / den : 0.f;
+      const float lse = (OP == kLogSoftmax) ? logf(den) : 0.f;
+      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
+        float v[kUnroll][8];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], -INFINITY);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t g = g0 + u * TEAM;
+          if (g < groups) {
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if constexpr (OP == kSoftmax)
+                o[j] = ((mx == -INFINITY) ? 0.f : __expf(v[u][j] - mx)) * inv;
+              else
+                o[j] = v[u][j] - mx - lse;
+            }
+            store_group(out, g, n, o);
+          }
         }
       }
     }
@@ -212,15 +271,104 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
     for (int q = 0; q < RMAX; ++q) {
       const int64_t g = t + static_cast<int64_t>(q) * TEAM;
       if (g < groups) {
+        float o[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int64_t idx = g * 8 + j;
-          if (idx < n) {
-            const float o = LOG ? (v[q][j] - mx - lse) : v[q][j] * inv;
-            out[idx] = from_f32<TO>(o);
-          }
+        for (int j = 0; j < 8; ++j) o[j] = LOG ? (v[q][j] - mx - lse) : v[q][j] * inv;
+        store_group(out, g, n, o);
+      }
+    }
+  }
+}
+
+// Softmax / log-softmax of long rows (vocabulary-sized) by a cluster of CS
+// CTAs of kClusterTeam threads per row.  CTA c of the cluster owns the
+// contiguous groups [c*gpc, (c+1)*gpc) (gpc = ceil(groups / CS)) and keeps them
+// in registers: thread t holds local groups t, t + kClusterTeam, ... (at most
+// RMAX).  The row maximum and the sum of exponentials are combined across the
+// cluster through distributed shared memory: every CTA writes its partial into
+// slot c of every CTA, and after the cluster barrier each CTA folds the CS
+// slots in increasing c.  CS, gpc and the trees depend on n only.
+constexpr int kClusterTeam = 512;
+
+template <typename TI, typename TO, bool LOG, int CS, int RMAX>
+__global__ void __launch_bounds__(kClusterTeam)
+    row_softmax_cluster_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t n) {
+  constexpr int TEAM = kClusterTeam;
+  __shared__ float scratch[TEAM / 32 + 1];
+  __shared__ float part_max[CS];
+  __shared__ float part_sum[CS];
+  const int t = threadIdx.x;
+  const uint32_t rank = cluster_ctarank();
+  const int64_t r = blockIdx.x / CS;
+  const int64_t groups = (n + 7) / 8;
+  const int64_t gpc = (groups + CS - 1) / CS;
+  const int64_t g_lo = static_cast<int64_t>(rank) * gpc;
+  const int64_t g_hi = g_lo + gpc < groups ? g_lo + gpc : groups;
+  const TI* row = x + r * n;
+  float v[RMAX][8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q) {
+    const int64_t g = g_lo + t + static_cast<int64_t>(q) * TEAM;
+    if (g < g_hi) {
+      load_group(row, g, n, v[q], -INFINITY);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[q][j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q][j] = -INFINITY;
+    }
+  }
+  mx = team_reduce<TEAM, true>(mx, scratch);
+  if (t < CS) {
+    const uint32_t dst = mapa_shared(static_cast<uint32_t>(__cvta_generic_to_shared(&part_max[rank])),
+                                     static_cast<uint32_t>(t));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(mx) : "memory");
+  }
+  cluster_sync_all();
+  mx = part_max[0];
+#pragma unroll
+  for (int c = 1; c < CS; ++c) mx = fmaxf(mx, part_max[c]);
+  float den = 0.f;
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q) {
+    const int64_t g = g_lo + t + static_cast<int64_t>(q) * TEAM;
+    if (g < g_hi) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (g * 8 + j < n) {
+          float e;
+          if (LOG)
+            e = __expf(v[q][j] - mx);
+          else
+            e = (mx == -INFINITY) ? 0.f : __expf(v[q][j] - mx);
+          den += e;
+          if (!LOG) v[q][j] = e;
         }
       }
+    }
+  }
+  den = team_reduce<TEAM, false>(den, scratch);
+  if (t < CS) {
+    const uint32_t dst = mapa_shared(static_cast<uint32_t>(__cvta_generic_to_shared(&part_sum[rank])),
+                                     static_cast<uint32_t>(t));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(den) : "memory");
+  }
+  cluster_sync_all();
+  den = part_sum[0];
+#pragma unroll
+  for (int c = 1; c < CS; ++c) den += part_sum[c];
+  TO* out = y + r * n;
+  const float lse = LOG ? logf(den) : 0.f;
+  const float inv = den != 0.f ? 1.f / den : 0.f;
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q) {
+    const int64_t g = g_lo + t + static_cast<int64_t>(q) * TEAM;
+    if (g < g_hi) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = LOG ? (v[q][j] - mx - lse) : v[q][j] * inv;
+      store_group(out, g, n, o);
     }
   }
 }
@@ -237,6 +385,7 @@ __global__ void __launch_bounds__(256)
     const TI* base = x + o * n * inner + i;
     if constexpr (OP == kMean || OP == kL2Norm) {
       float acc = 0.f;
+#pragma unroll 8
       for (int64_t j = 0; j < n; ++j) {
         const float v = to_f32(base[j * inner]);
         acc += (OP == kL2Norm) ? v * v : v;
@@ -287,6 +436,7 @@ __global__ void __launch_bounds__(256)
     if constexpr (OP == kMean || OP == kL2Norm) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll 8
       for (int64_t j = 0; j < n; ++j) {
         const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
         const TI* e = reinterpret_cast<const TI*>(&w);
@@ -307,12 +457,14 @@ __global__ void __launch_bounds__(256)
         mx[k] = -INFINITY;
         den[k] = 0.f;
       }
+#pragma unroll 8
       for (int64_t j = 0; j < n; ++j) {
         const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
         const TI* e = reinterpret_cast<const TI*>(&w);
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], to_f32(e[k]));
       }
+#pragma unroll 8
       for (int64_t j = 0; j < n; ++j) {
         const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
         const TI* e = reinterpret_cast<const TI*>(&w);
@@ -326,6 +478,7 @@ __global__ void __launch_bounds__(256)
         }
       }
       TO* out = y + o * n * inner + i0;
+#pragma unroll 8
       for (int64_t j = 0; j < n; ++j) {
         const uint4 w = *reinterpret_cast<const uint4*>(base + j * inner);
         const TI* e = reinterpret_cast<const TI*>(&w);
@@ -355,6 +508,44 @@ int team_for(int64_t n) {
   if (n <= 2048) return 32;
   if (n <= 32768) return 256;
   return 1024;
+}
+
+// Rows of (16384, kMaxClusterRow] elements: cluster softmax, CS CTAs per row.
+constexpr int kMaxClusterRow = 8 * bio::kClusterTeam * 8 * 8;
+
+template <typename TI, typename TO, bool LOG, int CS, int RMAX>
+int launch_cluster_case(const TI* x, TO* y, int64_t rows, int64_t n, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows * CS));
+  cfg.blockDim = dim3(bio::kClusterTeam);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return bio_host::launch_status(
+      cudaLaunchKernelEx(&cfg, bio::row_softmax_cluster_kernel<TI, TO, LOG, CS, RMAX>, x, y, n));
+}
+
+template <typename TI, typename TO, bool LOG>
+int launch_cluster_softmax(const TI* x, TO* y, int64_t rows, int64_t n, cudaStream_t stream) {
+  const int cs = n <= 4 * 16384 ? 2 : (n <= 8 * 16384 ? 4 : 8);
+  const int64_t groups = (n + 7) / 8;
+  const int64_t gpc = (groups + cs - 1) / cs;
+  const int64_t per = (gpc + bio::kClusterTeam - 1) / bio::kClusterTeam;
+  const int rmax = per <= 1 ? 1 : (per <= 2 ? 2 : (per <= 4 ? 4 : 8));
+#define BIO_CL_CASE(C, R) \
+  if (cs == C && rmax == R) return launch_cluster_case<TI, TO, LOG, C, R>(x, y, rows, n, stream);
+  BIO_CL_CASE(2, 4)
+  BIO_CL_CASE(2, 8)
+  BIO_CL_CASE(4, 8)
+  BIO_CL_CASE(8, 8)
+#undef BIO_CL_CASE
+  return BIO_ERR_ARG;
 }
 
 template <typename TI, typename TO, int OP>
@@ -387,6 +578,10 @@ int launch_rows(const void* x, void* y, int64_t outer, int64_t n, int64_t inner,
       BIO_REG_CASE(256, 4)
       BIO_REG_CASE(256, 8)
 #undef BIO_REG_CASE
+    }
+    if ((OP == bio::kSoftmax || OP == bio::kLogSoftmax) && n > 256 * 64 &&
+        n <= static_cast<int64_t>(kMaxClusterRow) && outer <= (int64_t{1} << 27)) {
+      return launch_cluster_softmax<TI, TO, OP == bio::kLogSoftmax>(xi, yo, outer, n, stream);
     }
     switch (team) {
       case 32: bio::row_kernel<TI, TO, OP, 32><<<g, 256, 0, stream>>>(xi, yo, outer, n); break;

@@ -191,3 +191,57 @@ def test_odd_shapes_and_empty():
         torch.testing.assert_close(out.double().cpu(), O.mm(a, b), rtol=2e-2, atol=2e-2)
     empty = matmul_persistent(torch.empty(0, 8, device="cuda"), torch.randn(8, 3, device="cuda"))
     assert empty.shape == (0, 3)
+
+
+# ------------------------------------------------------------------ tile independence
+# Every output tile runs the same per-element arithmetic (64-wide K blocks in
+# order, four K=16 tensor-core MMAs each, fp32 accumulator, one rounding), so
+# the tile shape -- one CTA (128 rows) or a CTA pair (256 rows), 32..256
+# columns -- must not change a single bit.  Inputs span 2^-8..2^8 in
+# magnitude so that accumulation order differences would show.
+_TILES_K_MAJOR = ((128, 32), (128, 64), (128, 128), (128, 256), (256, 128), (256, 256))
+_TILES_N_MAJOR = ((128, 64), (128, 128), (128, 256), (256, 128), (256, 256))
+
+
+def _wide(*shape, dtype, gen, span):
+    x = torch.randn(*shape, device="cuda", generator=gen)
+    e = torch.randint(-span, span + 1, shape, device="cuda", generator=gen).float()
+    return (x * torch.exp2(e)).to(dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", ((1, 200, 64), (37, 512, 1000), (300, 384, 4096), (129, 96, 72)))
+@pytest.mark.parametrize("b_layout", ("k_major", "n_major"))
+@pytest.mark.parametrize("with_bias", (False, True))
+def test_every_tile_shape_gives_identical_bits(dtype, m, n, k, b_layout, with_bias):
+    from batch_invariant_ops import _gemm
+
+    gen = torch.Generator(device="cuda").manual_seed(m * 7919 + n * 31 + k)
+    span = 8 if dtype == torch.bfloat16 else 3
+    a = _wide(m, k, dtype=dtype, gen=gen, span=span)
+    if b_layout == "k_major":
+        b = _wide(n, k, dtype=dtype, gen=gen, span=span).t()
+        tiles = _TILES_K_MAJOR
+    else:
+        b = _wide(k, n, dtype=dtype, gen=gen, span=span)
+        tiles = _TILES_N_MAJOR
+    bias = _wide(n, dtype=dtype, gen=gen, span=2) if with_bias else None
+    ref = _gemm.mm(a, b, bias, tile=(256, 256))
+    for tile in tiles:
+        out = _gemm.mm(a, b, bias, tile=tile)
+        assert torch.equal(out, ref), f"tile {tile} differs from (256, 256)"
+    expect = O.linear(a, b.t(), bias)
+    tol = dict(TOLERANCES[dtype])
+    scale = float(expect.abs().max()) + 1.0
+    torch.testing.assert_close(ref.double().cpu(), expect, rtol=tol["rtol"], atol=tol["atol"] * scale)
+
+
+def test_unsupported_tile_is_rejected():
+    from batch_invariant_ops import _gemm
+
+    a = torch.randn(4, 64, device="cuda").bfloat16()
+    b = torch.randn(64, 128, device="cuda").bfloat16()
+    with pytest.raises(RuntimeError):
+        _gemm.mm(a, b, tile=(128, 48))
+    with pytest.raises(RuntimeError):
+        _gemm.mm(a, b, tile=(128, 32))  # N-contiguous B needs tile_n >= 64

@@ -197,7 +197,12 @@ def test_softmax_and_log_softmax_match_torch(dtype, dim):
     _close_to_oracle(log_softmax(x, dim), O.log_softmax(x, dim), dtype)
 
 
-@pytest.mark.parametrize("n", (1, 7, 145, 2048, 2049, 4096, 40000, 257152))
+# Widths cover every row-mode kernel: one warp per row (n <= 2048), one CTA
+# per row with the row in registers (n <= 16384), a cluster of 2/4/8 CTAs per
+# row (n <= 262144) and the three-pass CTA kernel beyond; odd widths make
+# rows start off 16-byte boundaries (element loads and stores).
+@pytest.mark.parametrize("n", (1, 7, 145, 2048, 2049, 4096, 16384, 16385, 40000, 65536, 65537,
+                               70001, 131073, 257152, 262144, 262145, 300001))
 def test_softmax_row_widths_bitwise_invariant(n):
     gen = torch.Generator(device="cuda").manual_seed(n)
     x = _rn(9, n, dtype=torch.bfloat16, gen=gen)
@@ -206,7 +211,25 @@ def test_softmax_row_widths_bitwise_invariant(n):
     assert torch.equal(softmax(x[3:4], -1), full[3:4])
     lf = log_softmax(x, -1)
     assert torch.equal(log_softmax(x[:1], -1), lf[:1])
+    assert torch.equal(log_softmax(x[5:8], -1), lf[5:8])
     _close_to_oracle(full[:2], O.softmax(x[:2], -1), torch.bfloat16)
+    _close_to_oracle(lf[7:], O.log_softmax(x[7:], -1), torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", (torch.float32, torch.float16))
+@pytest.mark.parametrize("n", (30000, 100003, 257152))
+def test_softmax_cluster_rows_other_dtypes(dtype, n):
+    gen = torch.Generator(device="cuda").manual_seed(n + 3)
+    x = _rn(5, n, dtype=dtype, gen=gen) * 4
+    x[1, ::3] = -math.inf
+    full = softmax(x, -1)
+    assert torch.equal(softmax(x[1:2], -1), full[1:2])
+    _close_to_oracle(full, O.softmax(x, -1), dtype)
+    lf = log_softmax(x[2:], -1)
+    assert torch.equal(log_softmax(x[4:], -1), lf[2:])
+    _close_to_oracle(lf, O.log_softmax(x[2:], -1), dtype)
+    up = softmax(x, -1, dtype=torch.float32) if dtype != torch.float32 else full
+    _close_to_oracle(up, O.softmax(x, -1), torch.float32)
 
 
 def test_softmax_fully_masked_row_is_zero_and_output_dtype():
