@@ -739,14 +739,25 @@ def run_profile_point(args) -> None:
         print(json.dumps({"profile_point": args.profile_point, "launches": 1 + args.steps,
                           "checksum": float(y.float().sum().item())}))
         return
-    m, n = (int(v) for v in args.profile_point.split("x"))
+    # MxN (K = 4096, library tile) or MxNxK@TMxTN (explicit output tile)
+    spec, _, tile = args.profile_point.partition("@")
+    dims = [int(v) for v in spec.split("x")]
+    m, n = dims[0], dims[1]
+    k = dims[2] if len(dims) > 2 else K
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(0)
-    x = torch.randn(m, K, device=dev, generator=gen).to(torch.bfloat16)
-    w = (torch.randn(n, K, device=dev, generator=gen) / 64).to(torch.bfloat16)
+    x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=dev, generator=gen) / 64).to(torch.bfloat16)
     b = (torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
-    for _ in range(1 + args.steps):
-        y = linear_batch_invariant(x, w, b)
+    if tile:
+        from batch_invariant_ops import _gemm
+
+        t = tuple(int(v) for v in tile.split("x"))
+        for _ in range(1 + args.steps):
+            y = _gemm.mm(x, w.t(), b, tile=t)
+    else:
+        for _ in range(1 + args.steps):
+            y = linear_batch_invariant(x, w, b)
     torch.cuda.synchronize()
     print(json.dumps({"profile_point": args.profile_point, "launches": 1 + args.steps,
                       "checksum": float(y.float().sum().item())}))

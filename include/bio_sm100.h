@@ -111,9 +111,11 @@ typedef struct bio_gemm_args {
 
 BIO_API int bio_gemm(const bio_gemm_args* args, void* stream);
 
-/* Tile configuration id chosen for (n, k, dtype); exposed so tests can prove
- * that the schedule does not depend on m or the batch count.  Encodes
- * block_m * 1000000 + block_n * 1000 + block_k. */
+/* Configuration id for (n, k, dtype): the large-M output tile and the K block
+ * whose fixed order defines every output element's accumulation.  Encodes
+ * block_m * 1000000 + block_n * 1000 + block_k.  The output tile of a call
+ * may also depend on m (small m streams B with narrower tiles); all tiles run
+ * the same per-element sequence, which bio_gemm_tiled lets tests check. */
 BIO_API int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype);
 
 /* bio_gemm with an explicit output tile for the tensor-core path (f16/bf16):
