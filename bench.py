@@ -394,7 +394,7 @@ def run_ours(args) -> None:
             "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 3),
             "traffic": traffic,
-            "kernel": f"bio::gemm_tc_kernel tile {_gemm.tile_config(dn, K, torch.bfloat16)} at M={dm} N={dn} K={K}",
+            "kernel": f"bio::gemm_tc2_kernel (CTA pair) tile {_gemm.tile_config(dn, K, torch.bfloat16)} at M={dm} N={dn} K={K}",
             "peak_source": f"{peak_kind} bf16_tflops (burst); sustained {peaks.get('bf16_tflops_sustained')}",
             "algorithmic_flops_per_launch": _flops(dm, dn),
         }
