@@ -38,7 +38,6 @@ namespace bio {
 
 constexpr int kAtBM = 128;
 constexpr int kAtBN = 128;
-constexpr int kAtMaxThreads = 320;  // TMA, MMA, up to 8 softmax warps (2 per TMEM lane quarter)
 
 struct AttnTcParams {
   int64_t heads, kv_heads;
@@ -631,15 +630,550 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
   }
 }
 
-__global__ void attn_plan_kernel(const void* cu_q, int is64, int64_t nseq, int* blk_start) {
+__global__ void attn_plan_kernel(const void* cu_q, int is64, int64_t nseq, int bm,
+                                 int* blk_start) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int acc = 0;
   for (int64_t s = 0; s < nseq; ++s) {
     blk_start[s] = acc;
     const int64_t len = ld_off(cu_q, is64, s + 1) - ld_off(cu_q, is64, s);
-    if (len > 0) acc += static_cast<int>((len + kAtBM - 1) / kAtBM);
+    if (len > 0) acc += static_cast<int>((len + bm - 1) / bm);
   }
   blk_start[nseq] = acc;
+}
+
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA (D = Dv in {64, 128}).
+//
+// The CTA owns 256 query rows of one (sequence, head) as two tiles of 128.
+// Each tile has its own S buffer and O accumulator in TMEM (S_t at column
+// 128 t, O_t at 256 + D t) and its own softmax warpgroup (warps 2..5 tile 0,
+// 6..9 tile 1; one thread per query row, all 128 scores of a key block in
+// registers).  The MMA thread issues, per key block j,
+//     PV_0(j), S_0(j+1), PV_1(j), S_1(j+1)
+// so that the tensor core works on one tile while the other tile's softmax
+// runs.  tcgen05 operations of one thread complete in issue order, so the
+// arrival of S_t(j+1) also tells softmax t that PV_t(j) is done: its P
+// buffer may be rewritten and its O row rescaled.  K and V have separate
+// rings (K is consumed early by the S products, V late by the PV products).
+//
+// Per-row arithmetic is the same as in attn_tc_kernel's contract: keys in
+// fixed blocks of 128 from the first key of the sequence, a fixed tree per 32
+// scores, P rounded to the input dtype, the row sum taken over the rounded
+// P, the lazy rescale rule decided by the row's own scores.  Results depend
+// on the row's Q, the sequence's K/V and the block partition only.
+// ---------------------------------------------------------------------------
+constexpr int kAt2BM = 256;
+constexpr int kAt2Threads = 320;
+
+template <int D>
+struct Attn2Smem {
+  static constexpr uint32_t kQ = 128 * D * 2;  // one tile
+  static constexpr uint32_t kK = kAtBN * D * 2;
+  static constexpr uint32_t kV = kAtBN * D * 2;
+  static constexpr uint32_t kP = 128 * kAtBN * 2;  // one tile
+  static constexpr int kKS = D == 128 ? 2 : 4;
+  static constexpr int kVS = D == 128 ? 1 : 4;
+  static constexpr uint32_t kBar = 256;
+  static constexpr uint32_t kTotal = 1024 + 2 * kQ + 2 * kP + kKS * kK + kVS * kV + kBar;
+  static_assert(kTotal <= 227u * 1024u, "attention smem plan exceeds 227 KB");
+};
+
+// Scale and mask one 32-column chunk of a row's scores in place (raw words
+// in, scaled + masked fp32 words out; columns >= lim become -inf).  A chunk
+// that lies inside the key range of a unit-stride, 16-byte aligned mask row
+// is read with 16-byte loads; anything else element by element.
+__device__ __forceinline__ void apply_mask_chunk(const AttnTcParams& p, uint32_t (&f)[32],
+                                                 int64_t mrow, int64_t col, int lim,
+                                                 int64_t lk_seq) {
+  const int esz = p.mask_kind == 1 ? 1 : (p.mask_kind == 2 ? 4 : 2);
+  const uint8_t* mp = static_cast<const uint8_t*>(p.mask) + (mrow + col * p.m_sk) * esz;
+  const bool vec = p.m_sk == 1 && col + 32 <= lk_seq &&
+                   (reinterpret_cast<uintptr_t>(mp) & 15u) == 0;
+  if (vec) {
+    if (p.mask_kind == 1) {
+      const uint4 w0 = reinterpret_cast<const uint4*>(mp)[0];
+      const uint4 w1 = reinterpret_cast<const uint4*>(mp)[1];
+      const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const bool keep = ((wd[j >> 2] >> ((j & 3) * 8)) & 0xffu) != 0;
+        const float sv = (j < lim && keep) ? __uint_as_float(f[j]) * p.scale : -INFINITY;
+        f[j] = __float_as_uint(sv);
+      }
+    } else if (p.mask_kind == 2) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 a = reinterpret_cast<const float4*>(mp)[q];
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = q * 4 + e;
+          f[j] = __float_as_uint(j < lim ? fmaf(__uint_as_float(f[j]), p.scale, av[e])
+                                         : -INFINITY);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 a = reinterpret_cast<const uint4*>(mp)[q];
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float lo, hi;
+          if (p.mask_kind == 3) {
+            unpack_pair<__half>(aw[e], lo, hi);
+          } else {
+            unpack_pair<__nv_bfloat16>(aw[e], lo, hi);
+          }
+          const int j = q * 8 + 2 * e;
+          f[j] = __float_as_uint(j < lim ? __uint_as_float(f[j]) * p.scale + lo : -INFINITY);
+          f[j + 1] = __float_as_uint(j + 1 < lim ? __uint_as_float(f[j + 1]) * p.scale + hi
+                                                 : -INFINITY);
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 4
+  for (int j = 0; j < 32; ++j) {
+    float sv = -INFINITY;
+    if (j < lim) {
+      sv = __uint_as_float(f[j]) * p.scale;
+      const int64_t idx = mrow + (col + j) * p.m_sk;
+      if (p.mask_kind == 1) {
+        if (static_cast<const uint8_t*>(p.mask)[idx] == 0) sv = -INFINITY;
+      } else {
+        sv += mask_add(p.mask, p.mask_kind, idx);
+      }
+    }
+    f[j] = __float_as_uint(sv);
+  }
+}
+
+template <int D, typename T>
+__global__ void __launch_bounds__(kAt2Threads, 1)
+    attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
+  using L = Attn2Smem<D>;
+  constexpr int KS = L::kKS;
+  constexpr int VS = L::kVS;
+  constexpr int kChunks = D / 64;
+  constexpr uint32_t kIdescS = idesc_f16(AtFmt<T>::v, 128, kAtBN, false, false);
+  constexpr uint32_t kIdescO = idesc_f16(AtFmt<T>::v, 128, D, false, true);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---------------------------------------------------------------- work
+  int64_t b = 0, h = blockIdx.y, q0, lq_seq, lk_seq, q_tok0, k_tok0;
+  if (p.varlen) {
+    const int64_t g = blockIdx.x;
+    const int64_t total = p.blk_start[p.nseq];
+    if (g >= total) return;
+    int64_t lo = 0, hi = p.nseq;
+    while (hi - lo > 1) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (p.blk_start[mid] <= g) lo = mid; else hi = mid;
+    }
+    const int64_t sq = lo;
+    const int64_t qs0 = ld_off(p.cu_q, p.cu_is64, sq), qs1 = ld_off(p.cu_q, p.cu_is64, sq + 1);
+    const int64_t ks0 = ld_off(p.cu_k, p.cu_is64, sq), ks1 = ld_off(p.cu_k, p.cu_is64, sq + 1);
+    const bool bad = qs0 < 0 || qs1 > p.lq || ks0 < 0 || ks1 < ks0 || ks1 > p.lk ||
+                     ld_off(p.cu_q, p.cu_is64, 0) != 0 || ld_off(p.cu_k, p.cu_is64, 0) != 0 ||
+                     (p.causal == 3 && (qs1 - qs0) != (ks1 - ks0));
+    if (bad) {
+      if (threadIdx.x == 0) raise_status(p.status, BIO_DEV_INDEX);
+      return;  // output rows stay zero (pre-zeroed by the caller)
+    }
+    q0 = (g - p.blk_start[sq]) * kAt2BM;
+    lq_seq = qs1 - qs0;
+    lk_seq = ks1 - ks0;
+    q_tok0 = qs0 + q0;
+    k_tok0 = ks0;
+  } else {
+    b = blockIdx.z;
+    // heaviest (latest, for causal) query blocks first
+    q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * kAt2BM;
+    lq_seq = p.lq;
+    lk_seq = p.lk;
+    q_tok0 = q0;
+    k_tok0 = 0;
+  }
+  const int64_t hk = h / (p.heads / p.kv_heads);
+  const int64_t shift = (p.causal == 2) ? (lk_seq - lq_seq) : 0;
+  int nblk_t[2];
+  int64_t nrows_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int64_t first = q0 + 128 * t;
+    nrows_t[t] = max(static_cast<int64_t>(0), min(static_cast<int64_t>(128), lq_seq - first));
+    int64_t kend = lk_seq;
+    if (p.causal != 0) kend = min(lk_seq, first + nrows_t[t] - 1 + shift + 1);
+    if (nrows_t[t] == 0 || kend < 0) kend = 0;
+    nblk_t[t] = static_cast<int>((kend + kAtBN - 1) / kAtBN);
+  }
+  const int nblk = max(nblk_t[0], nblk_t[1]);
+
+  // softmax role: tile, row
+  const int tt = (warp - 2) >> 2;  // 0 or 1 for warps 2..9
+  const int qtr = warp & 3;
+  const int r = qtr * 32 + lane;
+  const int64_t i = q0 + 128 * (warp >= 2 ? tt : 0) + r;
+  const bool row_valid = warp >= 2 && r < nrows_t[warp >= 2 ? tt : 0];
+  T* out_row = nullptr;
+  if (row_valid) {
+    out_row = static_cast<T*>(p.o) + (p.varlen ? 0 : b * p.o_sb) + h * p.o_sh +
+              (p.varlen ? (q_tok0 + 128 * tt + r) : i) * p.o_st;
+  }
+  if (nblk == 0) {
+    if (row_valid)
+      for (int c = 0; c < p.dv; ++c) out_row[c] = from_f32<T>(0.f);
+    return;
+  }
+
+  // ---------------------------------------------------------------- smem
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;                 // [2][kQ]
+  uint8_t* sP = sQ + 2 * L::kQ;       // [2][kP]
+  uint8_t* sK = sP + 2 * L::kP;       // [KS][kK]
+  uint8_t* sV = sK + KS * L::kK;      // [VS][kV]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * L::kV);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;             // [KS]
+  uint64_t* k_empty = k_full + KS;         // [KS]
+  uint64_t* v_full = k_empty + KS;         // [VS]
+  uint64_t* v_empty = v_full + VS;         // [VS]
+  uint64_t* s_full = v_empty + VS;         // [2]
+  uint64_t* p_ready = s_full + 2;          // [2]
+  uint64_t* o_done = p_ready + 2;          // [2]
+  uint64_t* mma_done = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int qc = static_cast<int>(q_tok0), kc0 = static_cast<int>(k_tok0);
+  const int hc = static_cast<int>(h), hkc = static_cast<int>(hk), bc = static_cast<int>(b);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      mbar_arrive_expect_tx(q_full, 2 * L::kQ);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < kChunks; ++c)
+          tma_load_4d(sQ + t * L::kQ + c * 16384, &tmQ, q_full, c * 64, qc + 128 * t, hc, bc);
+      // K runs one block ahead of V: K_{j+1} is issued before V_j waits for
+      // the PV products of block j-1 to release its slot.
+      int k_issued = 0, v_issued = 0;
+      auto load_k = [&](int jb) -> bool {
+        const int ks = jb % KS;
+        if (!at_wait(&k_empty[ks], (static_cast<uint32_t>(jb / KS) & 1u) ^ 1u, abort_flag,
+                     p.status))
+          return false;
+        mbar_arrive_expect_tx(&k_full[ks], L::kK);
+        for (int c = 0; c < kChunks; ++c)
+          tma_load_4d(sK + ks * L::kK + c * 16384, &tmK, &k_full[ks], c * 64,
+                      kc0 + jb * kAtBN, hkc, bc);
+        k_issued = jb + 1;
+        return true;
+      };
+      bool okp = load_k(0);
+      for (int jb = 0; okp && jb < nblk; ++jb) {
+        if (jb + 1 < nblk && !load_k(jb + 1)) break;
+        const int vs = jb % VS;
+        if (!at_wait(&v_empty[vs], (static_cast<uint32_t>(jb / VS) & 1u) ^ 1u, abort_flag,
+                     p.status))
+          break;
+        mbar_arrive_expect_tx(&v_full[vs], L::kV);
+        const int row = kc0 + jb * kAtBN;
+        for (int kcnk = 0; kcnk < 2; ++kcnk)
+          for (int nc = 0; nc < kChunks; ++nc)
+            tma_load_4d(sV + vs * L::kV + (kcnk * kChunks + nc) * 8192, &tmV, &v_full[vs],
+                        nc * 64, row + kcnk * 64, hkc, bc);
+        v_issued = jb + 1;
+      }
+      // drain: Q and the last copies of every ring slot land before exit
+      if (!at_wait_drain(q_full, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+      for (int jb = k_issued - 1; jb >= 0 && jb >= k_issued - KS; --jb)
+        if (!at_wait_drain(&k_full[jb % KS], static_cast<uint32_t>(jb / KS) & 1u))
+          raise_status(p.status, BIO_DEV_TIMEOUT);
+      for (int jb = v_issued - 1; jb >= 0 && jb >= v_issued - VS; --jb)
+        if (!at_wait_drain(&v_full[jb % VS], static_cast<uint32_t>(jb / VS) & 1u))
+          raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA
+      bool ok = at_wait(q_full, 0, abort_flag, p.status);
+      auto issue_s = [&](int t, int jb) -> bool {
+        const int ks = jb % KS;
+        if (!at_wait(&k_full[ks], static_cast<uint32_t>(jb / KS) & 1u, abort_flag, p.status))
+          return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ + t * L::kQ), ka = smem_u32(sK + ks * L::kK);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16(tmem + static_cast<uint32_t>(t * 128), smem_desc_sw128(qa + off, 16, 1024),
+                   smem_desc_sw128(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+        return true;
+      };
+      auto issue_pv = [&](int t, int jb) -> bool {
+        if (!at_wait(&p_ready[t], static_cast<uint32_t>(jb) & 1u, abort_flag, p.status))
+          return false;
+        const int vs = jb % VS;
+        if (!at_wait(&v_full[vs], static_cast<uint32_t>(jb / VS) & 1u, abort_flag, p.status))
+          return false;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP + t * L::kP), va = smem_u32(sV + vs * L::kV);
+#pragma unroll
+        for (int kk = 0; kk < kAtBN / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t boff = (kk >> 2) * (kChunks * 8192) + (kk & 3) * 2048;
+          umma_f16(tmem + 256u + static_cast<uint32_t>(t * D), smem_desc_sw128(pa + aoff, 16, 1024),
+                   smem_desc_sw128(va + boff, 8192, 1024), kIdescO, (jb | kk) != 0 ? 1u : 0u);
+        }
+        if (jb == nblk_t[t] - 1) umma_commit(&o_done[t]);
+        return true;
+      };
+      if (ok && nblk_t[0] > 0) ok = issue_s(0, 0);
+      if (ok && nblk_t[1] > 0) ok = issue_s(1, 0);
+      if (ok) umma_commit(&k_empty[0]);
+      for (int jb = 0; ok && jb < nblk; ++jb) {
+#pragma unroll 1
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (jb < nblk_t[t]) ok = issue_pv(t, jb);
+          if (ok && jb + 1 < nblk_t[t]) ok = issue_s(t, jb + 1);
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[jb % VS]);
+        if (jb + 1 < nblk) umma_commit(&k_empty[(jb + 1) % KS]);
+      }
+      umma_commit(mma_done);
+      if (!at_wait_drain(mma_done, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int t = tt;
+    const int my_nblk = nblk_t[t];
+    const uint32_t lane_base = static_cast<uint32_t>(qtr * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + static_cast<uint32_t>(t * 128);
+    const uint32_t o_addr = tmem + lane_base + 256u + static_cast<uint32_t>(t * D);
+    int64_t kr = lk_seq;  // keys visible to this row
+    if (p.causal != 0) kr = min(lk_seq, i + shift + 1);
+    if (!row_valid || kr < 0) kr = 0;
+    const int64_t mrow = (p.mask_kind != 0 && row_valid)
+                             ? b * p.m_sb + h * p.m_sh + i * p.m_sq
+                             : 0;
+    // Without masks and with a positive scale the row maximum is taken on the
+    // raw scores (scaling is monotonic) and the scale folds into the exponent.
+    const bool plain = p.mask_kind == 0 && p.scale > 0.f;
+    const float kLog2e = 1.4426950408889634f;
+    const float cexp = plain ? p.scale * kLog2e : kLog2e;  // exponent factor of the domain
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint8_t* sPt = sP + t * L::kP;
+    for (int jb = 0; jb < my_nblk; ++jb) {
+      const bool got = at_wait(&s_full[t], static_cast<uint32_t>(jb) & 1u, abort_flag, p.status);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int64_t col0 = static_cast<int64_t>(jb) * kAtBN;
+      const int nvis = static_cast<int>(max(static_cast<int64_t>(0),
+                                            min(static_cast<int64_t>(kAtBN), kr - col0)));
+      // ---- scores of the block: four 32-column TMEM loads, one wait; kept
+      // as raw 32-bit words and rewritten in place
+      uint32_t f[4][32];
+      tmem_ld_32x32b_x32(s_addr + 0u, f[0]);
+      tmem_ld_32x32b_x32(s_addr + 32u, f[1]);
+      tmem_ld_32x32b_x32(s_addr + 64u, f[2]);
+      tmem_ld_32x32b_x32(s_addr + 96u, f[3]);
+      tmem_ld_wait();
+      const uint32_t kNegInf = 0xff800000u;
+      if (!plain) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) apply_mask_chunk(p, f[c], mrow, col0 + c * 32,
+                                                     nvis - c * 32, lk_seq);
+      } else if (nvis < kAtBN) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c * 32 + j >= nvis) f[c][j] = kNegInf;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float t16[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          t16[j] = fmaxf(__uint_as_float(f[c][2 * j]), __uint_as_float(f[c][2 * j + 1]));
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[2 * j], t16[2 * j + 1]);
+        mx = fmaxf(mx, t16[0]);
+      }
+      // Lazy reference point: m moves only when the block maximum exceeds it
+      // by more than 8 in log2 units (decided by this row's scores alone).
+      const bool move = (m == -INFINITY) ? (mx != -INFINITY) : ((mx - m) * cexp > 8.f);
+      const float m_new = move ? mx : m;
+      const float alpha = (m == -INFINITY || !move) ? 1.f : ex2_approx((m - m_new) * cexp);
+      // O_t holds PV_t(jb-1) (complete: S_t(jb) arrived after it)
+      if (jb > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(o_addr + static_cast<uint32_t>(c * 32), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
+          tmem_st_32x32b_x32(o_addr + static_cast<uint32_t>(c * 32), v);
+        }
+        tmem_st_wait();
+      }
+      // ---- P = exp2((x - m) * c) rounded to the input dtype, summed per
+      // 32-column chunk with a fixed tree (chunks in order), written into the
+      // 128-byte-swizzled K-major P tile of this query tile
+      const float mc = (m_new == -INFINITY) ? 0.f : m_new * cexp;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t w16[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float x0 = ex2_approx(fmaf(__uint_as_float(f[c][j]), cexp, -mc));
+          const float x1 = ex2_approx(fmaf(__uint_as_float(f[c][j + 1]), cexp, -mc));
+          w16[j / 2] = pack_pair<T>(x0, x1);
+        }
+        float t16[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float lo, hi;
+          unpack_pair<T>(w16[j], lo, hi);
+          t16[j] = lo + hi;
+        }
+        lsum += tree_sum16(t16);
+        uint8_t* base = sPt + (c >> 1) * 16384 + r * 128;
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int u = (c & 1) * 4 + u4;
+          *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) =
+              make_uint4(w16[u4 * 4 + 0], w16[u4 * 4 + 1], w16[u4 * 4 + 2], w16[u4 * 4 + 3]);
+        }
+      }
+      if (m_new != -INFINITY) {
+        l = l * alpha + lsum;
+        m = m_new;
+      }
+      // Zero V rows of a partial block that lie past the sequence end (they
+      // may belong to the next packed sequence); both tiles write the same
+      // zeros.
+      if (p.varlen && col0 + kAtBN > lk_seq) {
+        const int vs = jb % VS;
+        const bool vok = at_wait(&v_full[vs], static_cast<uint32_t>(jb / VS) & 1u, abort_flag,
+                                 p.status);
+        if (!__all_sync(0xffffffffu, vok)) {
+          ok = false;
+          break;
+        }
+        uint8_t* vt = sV + vs * L::kV;
+        const int first = static_cast<int>(lk_seq - col0);
+        for (int row = first + r; row < kAtBN; row += 128) {
+          const int kcnk = row >> 6, rr = row & 63;
+          for (int nc = 0; nc < kChunks; ++nc) {
+            uint4* dst = reinterpret_cast<uint4*>(vt + (kcnk * kChunks + nc) * 8192 + rr * 128);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) dst[u] = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_ready[t]);
+    }
+    if (ok && my_nblk > 0) {
+      const bool done = at_wait(&o_done[t], 0, abort_flag, p.status);
+      if (__all_sync(0xffffffffu, done)) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const bool vec = row_valid && p.dv == D &&
+                         (reinterpret_cast<uintptr_t>(out_row) & 15u) == 0;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(o_addr + static_cast<uint32_t>(c * 32), v);
+          tmem_ld_wait();
+          if (vec) {
+            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                w[e] = pack_pair<T>(__uint_as_float(v[q4 * 8 + 2 * e]) * inv,
+                                    __uint_as_float(v[q4 * 8 + 2 * e + 1]) * inv);
+              dst[q4] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else if (row_valid) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = c * 32 + j;
+              if (col < p.dv) out_row[col] = from_f32<T>(__uint_as_float(v[j]) * inv);
+            }
+          }
+        }
+      }
+    } else if (my_nblk == 0 && row_valid) {
+      for (int c = 0; c < p.dv; ++c) out_row[c] = from_f32<T>(0.f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
 }
 
 }  // namespace bio
@@ -711,6 +1245,43 @@ int launch_at(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const C
   }
   kern<<<grid, L::kThreads, L::kTotal, s>>>(q, k, v, p);
   return bio_host::launch_status(cudaGetLastError());
+}
+
+template <int D, typename T>
+int launch_at2(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const CUtensorMap& k,
+               const CUtensorMap& v, const bio::AttnTcParams& p, cudaStream_t s) {
+  using L = bio::Attn2Smem<D>;
+  auto kern = bio::attn_tc2_kernel<D, T>;
+  static bool attr_done[bio_host::kMaxDevices] = {false};
+  {
+    std::lock_guard<std::mutex> lk(g_at_mu);
+    if (!attr_done[a->device]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+          cudaSuccess)
+        return BIO_ERR_LAUNCH;
+      attr_done[a->device] = true;
+    }
+  }
+  dim3 grid;
+  if (varlen) {
+    const int64_t g = (a->lq + bio::kAt2BM - 1) / bio::kAt2BM + a->nseq;
+    if (g > 2147483647) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads), 1);
+  } else {
+    const int64_t g = (a->lq + bio::kAt2BM - 1) / bio::kAt2BM;
+    if (g > 2147483647 || a->batch > 65535 || a->heads > 65535) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads),
+                static_cast<unsigned>(a->batch));
+  }
+  kern<<<grid, bio::kAt2Threads, L::kTotal, s>>>(q, k, v, p);
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+// Two-tile kernel for D = Dv in {64, 128} when a CTA's second tile has rows
+// to work on (dense: more than 128 queries; varlen: always).
+bool use_two_tiles(int dp, int dvp, const bio_attn_args* a, bool varlen) {
+  if (dp != dvp || (dp != 64 && dp != 128)) return false;
+  return varlen || a->lq > bio::kAtBM;
 }
 
 template <typename T>
@@ -790,11 +1361,21 @@ int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream) {
   p.blk_start = static_cast<const int*>(a->workspace);
   p.status = bio_host::status_word(a->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool two = use_two_tiles(dp, dvp, a, varlen);
   if (varlen) {
     bio::attn_plan_kernel<<<1, 32, 0, s>>>(a->cu_q, a->cu_is64, a->nseq,
+                                           two ? bio::kAt2BM : bio::kAtBM,
                                            static_cast<int*>(a->workspace));
     const int st = bio_host::launch_status(cudaGetLastError());
     if (st != BIO_OK) return st;
+  }
+  if (two) {
+    if (a->dtype == BIO_BF16) {
+      return dp == 64 ? launch_at2<64, __nv_bfloat16>(a, varlen, tq, tk, tv, p, s)
+                      : launch_at2<128, __nv_bfloat16>(a, varlen, tq, tk, tv, p, s);
+    }
+    return dp == 64 ? launch_at2<64, __half>(a, varlen, tq, tk, tv, p, s)
+                    : launch_at2<128, __half>(a, varlen, tq, tk, tv, p, s);
   }
   if (a->dtype == BIO_BF16) return dispatch_at<__nv_bfloat16>(dp, dvp, a, varlen, tq, tk, tv, p, s);
   return dispatch_at<__half>(dp, dvp, a, varlen, tq, tk, tv, p, s);
