@@ -679,6 +679,31 @@ struct Attn2Smem {
   static_assert(kTotal <= 227u * 1024u, "attention smem plan exceeds 227 KB");
 };
 
+// Element-by-element mask of one chunk (any mask stride); fully unrolled so
+// that the score words stay in registers.
+template <int KIND>
+__device__ __forceinline__ void mask_chunk_strided(uint32_t (&f)[32], const uint8_t* mp,
+                                                   int64_t step, int lim, float scale) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float sv = -INFINITY;
+    if (j < lim) {
+      sv = __uint_as_float(f[j]) * scale;
+      if (KIND == 1) {
+        if (*mp == 0) sv = -INFINITY;
+      } else if (KIND == 2) {
+        sv += *reinterpret_cast<const float*>(mp);
+      } else if (KIND == 3) {
+        sv += __half2float(*reinterpret_cast<const __half*>(mp));
+      } else {
+        sv += __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(mp));
+      }
+    }
+    f[j] = __float_as_uint(sv);
+    mp += step;
+  }
+}
+
 // Scale and mask one 32-column chunk of a row's scores in place (raw words
 // in, scaled + masked fp32 words out; columns >= lim become -inf).  A chunk
 // that lies inside the key range of a unit-stride, 16-byte aligned mask row
@@ -735,19 +760,12 @@ __device__ __forceinline__ void apply_mask_chunk(const AttnTcParams& p, uint32_t
     }
     return;
   }
-#pragma unroll 4
-  for (int j = 0; j < 32; ++j) {
-    float sv = -INFINITY;
-    if (j < lim) {
-      sv = __uint_as_float(f[j]) * p.scale;
-      const int64_t idx = mrow + (col + j) * p.m_sk;
-      if (p.mask_kind == 1) {
-        if (static_cast<const uint8_t*>(p.mask)[idx] == 0) sv = -INFINITY;
-      } else {
-        sv += mask_add(p.mask, p.mask_kind, idx);
-      }
-    }
-    f[j] = __float_as_uint(sv);
+  const int64_t step = p.m_sk * esz;
+  switch (p.mask_kind) {
+    case 1: mask_chunk_strided<1>(f, mp, step, lim, p.scale); break;
+    case 2: mask_chunk_strided<2>(f, mp, step, lim, p.scale); break;
+    case 3: mask_chunk_strided<3>(f, mp, step, lim, p.scale); break;
+    default: mask_chunk_strided<4>(f, mp, step, lim, p.scale); break;
   }
 }
 
@@ -802,25 +820,25 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
   }
   const int64_t hk = h / (p.heads / p.kv_heads);
   const int64_t shift = (p.causal == 2) ? (lk_seq - lq_seq) : 0;
-  int nblk_t[2];
-  int64_t nrows_t[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int64_t first = q0 + 128 * t;
-    nrows_t[t] = max(static_cast<int64_t>(0), min(static_cast<int64_t>(128), lq_seq - first));
+  auto tile_rows = [&](int t) -> int64_t {
+    return max(static_cast<int64_t>(0), min(static_cast<int64_t>(128), lq_seq - (q0 + 128 * t)));
+  };
+  auto tile_blocks = [&](int t) -> int {
+    const int64_t nr = tile_rows(t);
     int64_t kend = lk_seq;
-    if (p.causal != 0) kend = min(lk_seq, first + nrows_t[t] - 1 + shift + 1);
-    if (nrows_t[t] == 0 || kend < 0) kend = 0;
-    nblk_t[t] = static_cast<int>((kend + kAtBN - 1) / kAtBN);
-  }
-  const int nblk = max(nblk_t[0], nblk_t[1]);
+    if (p.causal != 0) kend = min(lk_seq, q0 + 128 * t + nr - 1 + shift + 1);
+    if (nr == 0 || kend < 0) kend = 0;
+    return static_cast<int>((kend + kAtBN - 1) / kAtBN);
+  };
+  const int nblk0 = tile_blocks(0), nblk1 = tile_blocks(1);
+  const int nblk = max(nblk0, nblk1);
 
   // softmax role: tile, row
   const int tt = (warp - 2) >> 2;  // 0 or 1 for warps 2..9
   const int qtr = warp & 3;
   const int r = qtr * 32 + lane;
   const int64_t i = q0 + 128 * (warp >= 2 ? tt : 0) + r;
-  const bool row_valid = warp >= 2 && r < nrows_t[warp >= 2 ? tt : 0];
+  const bool row_valid = warp >= 2 && r < tile_rows(warp >= 2 ? tt : 0);
   T* out_row = nullptr;
   if (row_valid) {
     out_row = static_cast<T*>(p.o) + (p.varlen ? 0 : b * p.o_sb) + h * p.o_sh +
@@ -968,17 +986,18 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
           umma_f16(tmem + 256u + static_cast<uint32_t>(t * D), smem_desc_sw128(pa + aoff, 16, 1024),
                    smem_desc_sw128(va + boff, 8192, 1024), kIdescO, (jb | kk) != 0 ? 1u : 0u);
         }
-        if (jb == nblk_t[t] - 1) umma_commit(&o_done[t]);
+        if (jb == (t == 0 ? nblk0 : nblk1) - 1) umma_commit(&o_done[t]);
         return true;
       };
-      if (ok && nblk_t[0] > 0) ok = issue_s(0, 0);
-      if (ok && nblk_t[1] > 0) ok = issue_s(1, 0);
+      if (ok && nblk0 > 0) ok = issue_s(0, 0);
+      if (ok && nblk1 > 0) ok = issue_s(1, 0);
       if (ok) umma_commit(&k_empty[0]);
       for (int jb = 0; ok && jb < nblk; ++jb) {
 #pragma unroll 1
         for (int t = 0; t < 2 && ok; ++t) {
-          if (jb < nblk_t[t]) ok = issue_pv(t, jb);
-          if (ok && jb + 1 < nblk_t[t]) ok = issue_s(t, jb + 1);
+          const int nbt = t == 0 ? nblk0 : nblk1;
+          if (jb < nbt) ok = issue_pv(t, jb);
+          if (ok && jb + 1 < nbt) ok = issue_s(t, jb + 1);
         }
         if (!ok) break;
         umma_commit(&v_empty[jb % VS]);
@@ -990,7 +1009,7 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
   } else {
     // -------------------------------------------------------------- softmax
     const int t = tt;
-    const int my_nblk = nblk_t[t];
+    const int my_nblk = t == 0 ? nblk0 : nblk1;
     const uint32_t lane_base = static_cast<uint32_t>(qtr * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + static_cast<uint32_t>(t * 128);
     const uint32_t o_addr = tmem + lane_base + 256u + static_cast<uint32_t>(t * D);
@@ -1020,6 +1039,20 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
                                             min(static_cast<int64_t>(kAtBN), kr - col0)));
       // ---- scores of the block: four 32-column TMEM loads, one wait; kept
       // as raw 32-bit words and rewritten in place
+      // Masked launches first rewrite the block's scores in TMEM (scaled,
+      // masked, -inf past the visible range), one 32-column chunk at a time,
+      // so the mask code never holds the whole row in registers.
+      if (!plain) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t g[32];
+          tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+          tmem_ld_wait();
+          apply_mask_chunk(p, g, mrow, col0 + c * 32, nvis - c * 32, lk_seq);
+          tmem_st_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+        }
+        tmem_st_wait();
+      }
       uint32_t f[4][32];
       tmem_ld_32x32b_x32(s_addr + 0u, f[0]);
       tmem_ld_32x32b_x32(s_addr + 32u, f[1]);
@@ -1027,11 +1060,7 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
       tmem_ld_32x32b_x32(s_addr + 96u, f[3]);
       tmem_ld_wait();
       const uint32_t kNegInf = 0xff800000u;
-      if (!plain) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) apply_mask_chunk(p, f[c], mrow, col0 + c * 32,
-                                                     nvis - c * 32, lk_seq);
-      } else if (nvis < kAtBN) {
+      if (plain && nvis < kAtBN) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
