@@ -666,6 +666,44 @@ __global__ void attn_plan_kernel(const void* cu_q, int is64, int64_t nseq, int b
 constexpr int kAt2BM = 256;
 constexpr int kAt2Threads = 320;
 
+// Packed fp32 pair helpers (sm_100 f32x2 arithmetic) and a 3-input maximum.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Maximum of 32 score words (exact, so the grouping does not matter).
+__device__ __forceinline__ float max32_words(const uint32_t (&f)[32]) {
+  float t[11];
+#pragma unroll
+  for (int j = 0; j < 10; ++j)
+    t[j] = fmax3(__uint_as_float(f[3 * j]), __uint_as_float(f[3 * j + 1]),
+                 __uint_as_float(f[3 * j + 2]));
+  t[10] = fmaxf(__uint_as_float(f[30]), __uint_as_float(f[31]));
+  const float u0 = fmax3(t[0], t[1], t[2]), u1 = fmax3(t[3], t[4], t[5]);
+  const float u2 = fmax3(t[6], t[7], t[8]), u3 = fmaxf(t[9], t[10]);
+  return fmaxf(fmax3(u0, u1, u2), u3);
+}
+
 template <int D>
 struct Attn2Smem {
   static constexpr uint32_t kQ = 128 * D * 2;  // one tile
@@ -1067,19 +1105,8 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
           for (int j = 0; j < 32; ++j)
             if (c * 32 + j >= nvis) f[c][j] = kNegInf;
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t16[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          t16[j] = fmaxf(__uint_as_float(f[c][2 * j]), __uint_as_float(f[c][2 * j + 1]));
-#pragma unroll
-        for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-          for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[2 * j], t16[2 * j + 1]);
-        mx = fmaxf(mx, t16[0]);
-      }
+      const float mx = fmaxf(fmax3(max32_words(f[0]), max32_words(f[1]), max32_words(f[2])),
+                             max32_words(f[3]));
       // Lazy reference point: m moves only when the block maximum exceeds it
       // by more than 8 in log2 units (decided by this row's scores alone).
       const bool move = (m == -INFINITY) ? (mx != -INFINITY) : ((mx - m) * cexp > 8.f);
@@ -1098,35 +1125,40 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
         }
         tmem_st_wait();
       }
-      // ---- P = exp2((x - m) * c) rounded to the input dtype, summed per
-      // 32-column chunk with a fixed tree (chunks in order), written into the
-      // 128-byte-swizzled K-major P tile of this query tile
+      // ---- P = exp2((x - m) * c) rounded to the input dtype and written into
+      // the 128-byte-swizzled K-major P tile of this query tile.  The row sum
+      // runs over the fp32 exponentials in a fixed order: per 32-column chunk
+      // two interleaved lanes (even / odd columns) accumulate in column
+      // order, then lane 0 + lane 1, then chunks in order.
       const float mc = (m_new == -INFINITY) ? 0.f : m_new * cexp;
+      const uint64_t c2 = f2_pack(cexp, cexp), nmc2 = f2_pack(-mc, -mc);
       float lsum = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t w16[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float x0 = ex2_approx(fmaf(__uint_as_float(f[c][j]), cexp, -mc));
-          const float x1 = ex2_approx(fmaf(__uint_as_float(f[c][j + 1]), cexp, -mc));
-          w16[j / 2] = pack_pair<T>(x0, x1);
-        }
-        float t16[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float lo, hi;
-          unpack_pair<T>(w16[j], lo, hi);
-          t16[j] = lo + hi;
-        }
-        lsum += tree_sum16(t16);
+        uint64_t acc = f2_pack(0.f, 0.f);
         uint8_t* base = sPt + (c >> 1) * 16384 + r * 128;
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = u4 * 8 + 2 * e;
+            float a0, a1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(f[c][j]), __uint_as_float(f[c][j + 1])),
+                             c2, nmc2),
+                      a0, a1);
+            const float x0 = ex2_approx(a0);
+            const float x1 = ex2_approx(a1);
+            w4[e] = pack_pair<T>(x0, x1);
+            acc = f2_add(acc, f2_pack(x0, x1));
+          }
           const int u = (c & 1) * 4 + u4;
           *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) =
-              make_uint4(w16[u4 * 4 + 0], w16[u4 * 4 + 1], w16[u4 * 4 + 2], w16[u4 * 4 + 3]);
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
+        float s0, s1;
+        f2_unpack(acc, s0, s1);
+        lsum += s0 + s1;
       }
       if (m_new != -INFINITY) {
         l = l * alpha + lsum;
