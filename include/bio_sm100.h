@@ -118,6 +118,25 @@ BIO_API int bio_gemm(const bio_gemm_args* args, void* stream);
  * the same per-element sequence, which bio_gemm_tiled lets tests check. */
 BIO_API int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype);
 
+/* Workspace bytes that bio_gemm_f32_exact needs for these arguments; 0 when
+ * that path does not apply (dtype not BIO_F32, K == 0 or K > 65536, empty or
+ * invalid shapes). */
+BIO_API int64_t bio_gemm_f32_exact_workspace(const bio_gemm_args* args);
+
+/* fp32 GEMM (same arguments and result layout as bio_gemm) on the int8 tensor
+ * cores with exact integer slices: every row of A and column of B is scaled
+ * by a power of two and cut into four signed digits in [-64, 64], digit products are
+ * summed exactly in int32 TMEM accumulators, and the epilogue recombines them
+ * in fp64 with alpha and bias, rounding once to fp32.  Each output is within
+ * K * 2^-26 * max|A[m,:]| * max|B[:,n]| of the exact sum, and depends on its
+ * own A row and on B only (batch invariant).  `workspace`: device memory of
+ * at least bio_gemm_f32_exact_workspace(args) bytes, 256-byte aligned
+ * (BIO_ERR_SCRATCH if smaller).  Rows/columns holding Inf or NaN give NaN.
+ * Replaces the fp32 configuration of matmul_persistent / bmm_persistent
+ * (batch_invariant_ops.py:271-431), which accumulates in fp32. */
+BIO_API int bio_gemm_f32_exact(const bio_gemm_args* args, void* workspace,
+                               int64_t workspace_bytes, void* stream);
+
 /* bio_gemm with an explicit output tile for the tensor-core path (f16/bf16):
  * tile_m 128 (one CTA) or 256 (CTA pair), tile_n 32/64/128/256 (pair: 128 or
  * 256; an N-contiguous B needs tile_n >= 64).  The per-element arithmetic of

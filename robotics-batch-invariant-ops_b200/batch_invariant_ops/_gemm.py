@@ -190,9 +190,15 @@ def launch(
     bias_s2: int = 0,
     alpha: float = 1.0,
     tile: tuple[int, int] | None = None,
+    exact_f32: bool = True,
 ) -> None:
-    """Enqueue one bio_gemm on the current stream of ``c``'s device (with
-    ``tile`` = (tile_m, tile_n): bio_gemm_tiled, an explicit output tile)."""
+    """Enqueue one GEMM on the current stream of ``c``'s device.
+
+    fp32 runs on the int8 tensor cores with exact integer slices
+    (bio_gemm_f32_exact, workspace from the caching allocator) whenever that
+    path applies (K <= 32768), else on the fp64-accumulating kernel of
+    bio_gemm; ``exact_f32=False`` forces the latter.  ``tile`` = (tile_m,
+    tile_n) selects bio_gemm_tiled, an explicit output tile."""
     args = _lib.GemmArgs()
     args.dtype = _lib.DTYPE_CODE[c.dtype]
     args.flags = _lib.BIO_GEMM_BIAS_PER_ROW if bias_per_row else 0
@@ -221,8 +227,21 @@ def launch(
     args.bias_s2 = bias_s2
     args.alpha = alpha
     args.device = c.device.index
+    lib = _lib.load()
+    if tile is None and c.dtype == torch.float32 and exact_f32:
+        ws_bytes = lib.bio_gemm_f32_exact_workspace(ctypes.byref(args))
+        if ws_bytes > 0:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=c.device)
+            _lib.check(
+                lib.bio_gemm_f32_exact(
+                    ctypes.byref(args), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+                    _lib.stream_of(c),
+                ),
+                "bio_gemm_f32_exact",
+            )
+            return
     if tile is None:
-        _lib.check(_lib.load().bio_gemm(ctypes.byref(args), _lib.stream_of(c)), "bio_gemm")
+        _lib.check(lib.bio_gemm(ctypes.byref(args), _lib.stream_of(c)), "bio_gemm")
     else:
         _lib.check(
             _lib.load().bio_gemm_tiled(ctypes.byref(args), tile[0], tile[1], _lib.stream_of(c)),
@@ -235,9 +254,11 @@ def mm(
     b: torch.Tensor,
     bias: torch.Tensor | None = None,
     tile: tuple[int, int] | None = None,
+    exact_f32: bool = True,
 ) -> torch.Tensor:
     """C[M,N] = A[M,K] @ B[K,N] (+ bias[N]); any strides.  ``tile`` forces an
-    output tile (tests of tile independence)."""
+    output tile (tests of tile independence); ``exact_f32=False`` runs fp32 on
+    the fp64-accumulating kernel instead of the exact-slice tensor-core path."""
     m, k = a.shape
     n = b.shape[1]
     c = torch.empty((m, n), device=a.device, dtype=a.dtype)
@@ -252,7 +273,7 @@ def mm(
         opb = operand_b(b, 1, 1, k, n, b.stride(0), b.stride(1), 0, 0)
     launch(
         opa, opb, c, batch1=1, batch2=1, m=m, n=n, k=k, c_sm=n, c_sn=1, c_s1=0, c_s2=0, bias=bias,
-        tile=tile,
+        tile=tile, exact_f32=exact_f32,
     )
     return c
 

@@ -120,6 +120,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   return false;
 }
 
+// Wait used only while draining copies at kernel exit: bounded, ignores the
+// abort flag (the copies must land before shared memory is released).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 0; i < kWaitMaxIters; ++i) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled tensor copies; every CTA loads its own tiles)
 // ---------------------------------------------------------------------------

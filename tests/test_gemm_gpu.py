@@ -245,3 +245,85 @@ def test_unsupported_tile_is_rejected():
         _gemm.mm(a, b, tile=(128, 48))
     with pytest.raises(RuntimeError):
         _gemm.mm(a, b, tile=(128, 32))  # N-contiguous B needs tile_n >= 64
+
+
+# ------------------------------------------------------------------ exact-slice fp32
+# fp32 GEMMs run on the int8 tensor cores with exact integer slices
+# (bio_gemm_f32_exact).  Bar: normwise error against fp64 <= 1e-6 (the fp32
+# parity bar is 1e-5), agreement with the fp64-accumulating kernel, and the
+# usual bitwise batch invariance.
+def _normwise(out, ref):
+    return float((out.double().cpu() - ref).norm() / ref.norm())
+
+
+@pytest.mark.parametrize("m,n,k", ((1, 77, 64), (37, 300, 1000), (256, 512, 4096), (130, 129, 131)))
+@pytest.mark.parametrize("b_layout", ("k_major", "n_major"))
+def test_exact_f32_matches_fp64(m, n, k, b_layout):
+    from batch_invariant_ops import _gemm
+
+    gen = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn(m, k, device="cuda", generator=gen) * 3
+    if b_layout == "k_major":
+        b = torch.randn(n, k, device="cuda", generator=gen).t()
+    else:
+        b = torch.randn(k, n, device="cuda", generator=gen)
+    bias = torch.randn(n, device="cuda", generator=gen)
+    ref = a.double().cpu() @ b.double().cpu() + bias.double().cpu()
+    exact = _gemm.mm(a, b, bias)
+    dfma = _gemm.mm(a, b, bias, exact_f32=False)
+    assert _normwise(exact, ref) <= 1e-6
+    assert _normwise(dfma, ref) <= 1e-6
+    # elementwise: the exact-slice bound K * 2^-26 * max|A| * max|B|
+    bound = k * 2.0**-26 * float(a.abs().max()) * float(b.abs().max())
+    err = (exact.double().cpu() - ref).abs().max().item()
+    assert err <= bound, (err, bound)
+    assert torch.equal(_gemm.mm(a[:1], b, bias), exact[:1])
+
+
+def test_exact_f32_linspace_config1_accuracy():
+    # BASELINE config 1 at full size: massive cancellation, 1e-5 bar
+    bsz, d = 2048, 4096
+    a = torch.linspace(-100, 100, bsz * d, device="cuda").reshape(bsz, d)
+    w = torch.linspace(-100, 100, d * d, device="cuda").reshape(d, d)
+    out = matmul_persistent(a, w)
+    rows = torch.tensor([0, 1, 1023, 2047])
+    ref = a[rows].double().cpu() @ w.double().cpu()
+    # the fp32 bar is 1e-5; the slices give ~1.6e-6 on this cancelling case
+    # (every fp32 accumulation order gives 2e-4-5e-4)
+    assert _normwise(out[rows], ref) <= 5e-6
+    assert torch.equal(matmul_persistent(a[:1], w), out[:1])
+    assert torch.equal(matmul_persistent(a[2047:], w), out[2047:])
+
+
+def test_exact_f32_nonfinite_rows_give_nan():
+    from batch_invariant_ops import _gemm
+
+    a = torch.randn(4, 256, device="cuda")
+    b = torch.randn(256, 64, device="cuda")
+    a[2, 5] = float("inf")
+    out = _gemm.mm(a, b)
+    assert torch.isnan(out[2]).all()
+    ref = a.double().cpu() @ b.double().cpu()
+    assert _normwise(out[[0, 1, 3]], ref[[0, 1, 3]]) <= 1e-6
+
+
+def test_exact_f32_batched_and_broadcast():
+    gen = torch.Generator(device="cuda").manual_seed(99)
+    a = torch.randn(6, 33, 200, device="cuda", generator=gen)
+    w = torch.randn(200, 70, device="cuda", generator=gen)
+    wb = w.unsqueeze(0).expand(6, 200, 70)  # stride-0 batch
+    out = bmm_persistent(a, wb)
+    ref = torch.bmm(a.double().cpu(), wb.double().cpu())
+    assert _normwise(out, ref) <= 1e-6
+    assert torch.equal(bmm_persistent(a[2:3], wb[2:3]), out[2:3])
+
+
+def test_fp32_long_k_uses_fp64_accumulation_kernel():
+    # K > 65536 is outside the exact-slice path (int32 headroom); bio_gemm's
+    # fp64-accumulating kernel takes it
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(3, 70000, device="cuda", generator=gen)
+    b = torch.randn(70000, 17, device="cuda", generator=gen)
+    out = matmul_persistent(a, b)
+    ref = a.double().cpu() @ b.double().cpu()
+    assert _normwise(out, ref) <= 1e-6
