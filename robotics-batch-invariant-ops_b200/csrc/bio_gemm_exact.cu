@@ -41,7 +41,7 @@ constexpr int kXBM = 128;
 constexpr int kXBN = 128;
 constexpr int kXStages = 3;
 constexpr int kXPairs = 10;      // digit pairs with s + t <= 3
-constexpr int kXThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kXThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kXMaxK = 65536;
 
 // digit pair p -> (s, t); pairs are grouped by level s + t
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty, 4);
+    mbar_init(tempty, 8);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -420,7 +420,9 @@ __global__ void __launch_bounds__(kXThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // warps 2..9: TMEM lane quarter (warp & 3), column half (warp - 2) >> 2
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     uint32_t tphase = 0;
     for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       int64_t b1, b2;
@@ -437,36 +439,52 @@ __global__ void __launch_bounds__(kXThreads, 1)
       const int ea = mvalid ? p.ea[ai * p.m + m] : 0;
       float* crow = p.c + b1 * p.c_s1 + b2 * p.c_s2 + static_cast<int64_t>(m) * p.c_sm;
       const float* bias = p.bias != nullptr ? p.bias + b2 * p.bias_s2 : nullptr;
+      const float brow = (bias != nullptr && p.bias_per_row && mvalid) ? bias[m] : 0.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kXBN; c0 += 32) {
+      for (int c0 = half * (kXBN / 2); c0 < (half + 1) * (kXBN / 2); c0 += 32) {
         uint32_t g0[32], g1[32], g2[32], g3[32];
         const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0);
         tmem_ld_32x32b_x32(base + 0 * kXBN, g0);
         tmem_ld_32x32b_x32(base + 1 * kXBN, g1);
         tmem_ld_32x32b_x32(base + 2 * kXBN, g2);
         tmem_ld_32x32b_x32(base + 3 * kXBN, g3);
-        tmem_ld_wait();
         const int n0 = nb * kXBN + c0;
-        if (mvalid && n0 < p.n) {
+        // column data of this chunk: lane j holds column n0 + j
+        const bool nlane = n0 + lane < p.n;
+        const int eb_l = nlane ? p.eb[bi * p.n + n0 + lane] : 0;
+        const float bcol_l = (bias != nullptr && !p.bias_per_row && nlane) ? bias[n0 + lane] : 0.f;
+        tmem_ld_wait();
+        if (n0 >= p.n) continue;
+        float out[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            if (n >= p.n) continue;
-            const int eb = p.eb[bi * p.n + n];
-            float out;
-            if (ea == kXNonFinite || eb == kXNonFinite) {
-              out = __int_as_float(0x7fc00000);
-            } else {
-              double v = static_cast<double>(static_cast<int>(g0[j])) * 0x1p-14;
-              v += static_cast<double>(static_cast<int>(g1[j])) * 0x1p-21;
-              v += static_cast<double>(static_cast<int>(g2[j])) * 0x1p-28;
-              v += static_cast<double>(static_cast<int>(g3[j])) * 0x1p-35;
-              v = ldexp(v, ea + eb) * static_cast<double>(p.alpha);
-              if (bias != nullptr)
-                v += static_cast<double>(p.bias_per_row ? bias[m] : bias[n]);
-              out = __double2float_rn(v);
-            }
-            crow[static_cast<int64_t>(n) * p.c_sn] = out;
+        for (int j = 0; j < 32; ++j) {
+          const int eb = __shfl_sync(0xffffffffu, eb_l, j);
+          const float bj = p.bias_per_row ? brow : __shfl_sync(0xffffffffu, bcol_l, j);
+          double v = fma(static_cast<double>(static_cast<int>(g1[j])), 0x1p-21,
+                         static_cast<double>(static_cast<int>(g0[j])) * 0x1p-14);
+          v = fma(static_cast<double>(static_cast<int>(g2[j])), 0x1p-28, v);
+          v = fma(static_cast<double>(static_cast<int>(g3[j])), 0x1p-35, v);
+          // 2^(ea + eb) built from its exponent bits (ldexp when out of range)
+          const int ex = ea + eb;
+          const double sc = (ex > -1000 && ex < 1000)
+                                ? __hiloint2double((ex + 1023) << 20, 0)
+                                : ldexp(1.0, ex > 0 ? 1100 : -1100);
+          v = fma(v * sc, static_cast<double>(p.alpha), static_cast<double>(bj));
+          out[j] = (ea == kXNonFinite || eb == kXNonFinite) ? __int_as_float(0x7fc00000)
+                                                            : __double2float_rn(v);
+        }
+        if (mvalid) {
+          const bool vec = p.c_sn == 1 && n0 + 32 <= p.n &&
+                           (reinterpret_cast<uintptr_t>(crow + n0) & 15u) == 0;
+          if (vec) {
+            float4* dst = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = out[j];
           }
         }
       }
