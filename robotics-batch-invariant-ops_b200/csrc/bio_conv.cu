@@ -76,6 +76,77 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Table-driven im2col for patch rows of at most kIm2colTable entries: each
+// CTA first tabulates, per patch column kk, the input offset of its tap
+// (channel, z0*dil0, z1*dil1, z2*dil2) and the three dilated tap positions;
+// a warp then fills one patch row with one table read, the bounds test (only
+// for rows that touch the padding) and one load per entry.
+constexpr int kIm2colTable = 2048;
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    im2col_table_kernel(const T* __restrict__ x, T* __restrict__ patches, Geom g, int k_real,
+                        int kpad, int64_t rows) {
+  __shared__ int toff[kIm2colTable];
+  __shared__ short tz[3][kIm2colTable];
+  const int k1 = static_cast<int>(g.kernel[1]), k2 = static_cast<int>(g.kernel[2]);
+  const int kvol = static_cast<int>(g.kernel[0]) * k1 * k2;
+  const int64_t in1 = g.in[1], in2 = g.in[2];
+  const int64_t in_vol = g.in[0] * in1 * in2;
+  for (int kk = threadIdx.x; kk < k_real; kk += blockDim.x) {
+    const int c = kk / kvol;
+    const int z = kk - c * kvol;
+    const int z0 = z / (k1 * k2), z1 = (z / k2) % k1, z2 = z % k2;
+    const int d0 = z0 * static_cast<int>(g.dilation[0]);
+    const int d1 = z1 * static_cast<int>(g.dilation[1]);
+    const int d2 = z2 * static_cast<int>(g.dilation[2]);
+    toff[kk] = static_cast<int>(c * in_vol + (d0 * in1 + d1) * in2 + d2);
+    tz[0][kk] = static_cast<short>(d0);
+    tz[1][kk] = static_cast<short>(d1);
+    tz[2][kk] = static_cast<short>(d2);
+  }
+  __syncthreads();
+  const int64_t L = g.out[0] * g.out[1] * g.out[2];
+  const int64_t cg = g.channels / g.groups;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  const int span0 = static_cast<int>((g.kernel[0] - 1) * g.dilation[0]);
+  const int span1 = static_cast<int>((g.kernel[1] - 1) * g.dilation[1]);
+  const int span2 = static_cast<int>((g.kernel[2] - 1) * g.dilation[2]);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+       row < rows; row += warps) {
+    const int64_t l = row % L;
+    const int64_t bg = row / L;
+    const int64_t grp = bg % g.groups;
+    const int64_t b = bg / g.groups;
+    const int64_t o2 = l % g.out[2];
+    const int64_t t = l / g.out[2];
+    const int64_t o1 = t % g.out[1];
+    const int64_t o0 = t / g.out[1];
+    const int64_t b0 = o0 * g.stride[0] - g.padding[0];
+    const int64_t b1 = o1 * g.stride[1] - g.padding[1];
+    const int64_t b2 = o2 * g.stride[2] - g.padding[2];
+    const bool interior = b0 >= 0 && b1 >= 0 && b2 >= 0 && b0 + span0 < g.in[0] &&
+                          b1 + span1 < in1 && b2 + span2 < in2;
+    const T* xs = x + (b * g.channels + grp * cg) * in_vol + (b0 * in1 + b1) * in2 + b2;
+    T* dst = patches + row * kpad;
+    if (interior) {
+      for (int kk = lane; kk < kpad; kk += 32)
+        dst[kk] = kk < k_real ? xs[toff[kk]] : from_f32<T>(0.f);
+    } else {
+      for (int kk = lane; kk < kpad; kk += 32) {
+        T v = from_f32<T>(0.f);
+        if (kk < k_real) {
+          const int64_t i0 = b0 + tz[0][kk], i1 = b1 + tz[1][kk], i2 = b2 + tz[2][kk];
+          if (i0 >= 0 && i0 < g.in[0] && i1 >= 0 && i1 < in1 && i2 >= 0 && i2 < in2)
+            v = xs[toff[kk]];
+        }
+        dst[kk] = v;
+      }
+    }
+  }
+}
+
 // One warp per (sample, channel) row; lanes walk the output positions, each
 // folding its taps in order k = 0..K-1 in fp32, bias added after the taps.
 template <typename T>
@@ -99,6 +170,44 @@ __global__ void __launch_bounds__(256)
       for (int k = 0; k < ksize; ++k) {
         const int64_t i = i0 + static_cast<int64_t>(k) * dil;
         if (i >= 0 && i < lin) acc += to_f32(xr[i]) * to_f32(wr[k]);
+      }
+      if (bias != nullptr) acc += bv;
+      yr[l] = from_f32<T>(acc);
+    }
+  }
+}
+
+// Depthwise 1-D convolution with the input row staged in shared memory: a
+// warp copies its (sample, channel) row with all loads in flight, then each
+// lane computes outputs from shared memory (same tap order k = 0..K-1 and
+// bias after the taps as depthwise_conv1d_kernel, so results are identical).
+template <typename T>
+__global__ void __launch_bounds__(256)
+    depthwise_conv1d_smem_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                 const T* __restrict__ bias, T* __restrict__ y, int64_t channels,
+                                 int lin, int lout, int ksize, int stride, int pad, int dil,
+                                 int64_t rows) {
+  extern __shared__ __align__(16) unsigned char dw_smem[];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  T* srow = reinterpret_cast<T*>(dw_smem) + static_cast<int64_t>(wid) * lin;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t bc = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + wid; bc < rows;
+       bc += warps) {
+    const int64_t c = bc % channels;
+    const T* xr = x + bc * lin;
+    __syncwarp();
+#pragma unroll 8
+    for (int i = lane; i < lin; i += 32) srow[i] = xr[i];
+    __syncwarp();
+    const T* wr = w + c * ksize;
+    const float bv = bias != nullptr ? to_f32(bias[c]) : 0.f;
+    T* yr = y + bc * lout;
+    for (int l = lane; l < lout; l += 32) {
+      float acc = 0.f;
+      const int i0 = l * stride - pad;
+      for (int k = 0; k < ksize; ++k) {
+        const int i = i0 + k * dil;
+        if (i >= 0 && i < lin) acc += to_f32(srow[i]) * to_f32(wr[k]);
       }
       if (bias != nullptr) acc += bv;
       yr[l] = from_f32<T>(acc);
@@ -141,6 +250,90 @@ __global__ void __launch_bounds__(256)
     int64_t i2 = lane / k2, z2 = lane - (lane / k2) * k2;
     for (int64_t X = lane; X < d2; X += 32) {
       float v = to_f32(srow[z2 * in_vol + i2]);
+      if (bias != nullptr) v += bv;
+      drow[X] = from_f32<T>(v);
+      i2 += step_i;
+      z2 += step_z;
+      if (z2 >= k2) {
+        z2 -= k2;
+        ++i2;
+      }
+    }
+  }
+}
+
+// One CTA per output channel plane (b, oc): the plane's kvol source rows
+// (contiguous in the GEMM output) are staged in shared memory with a padded
+// row stride (no bank conflicts between the k2 rows a warp reads), then every
+// warp writes output rows contiguously, (i2, z2) advancing by 32 per step.
+// 32-bit index arithmetic; used when the plane fits in shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    convt_plane_kernel(const T* __restrict__ src, const T* __restrict__ bias,
+                       T* __restrict__ dst, Geom g, int og, int srow) {
+  extern __shared__ __align__(16) unsigned char convt_smem[];
+  T* sm = reinterpret_cast<T*>(convt_smem);
+  const int k0 = static_cast<int>(g.kernel[0]), k1 = static_cast<int>(g.kernel[1]),
+            k2 = static_cast<int>(g.kernel[2]);
+  const int s1 = static_cast<int>(g.in[1]), s2 = static_cast<int>(g.in[2]);
+  const int in_vol = static_cast<int>(g.in[0]) * s1 * s2;
+  const int kvol = k0 * k1 * k2;
+  const int d1 = s1 * k1, d2 = s2 * k2;
+  const int rows = static_cast<int>(g.in[0]) * k0 * d1;  // output rows of the plane
+  const int cout = og * static_cast<int>(g.groups);
+  const int64_t plane = blockIdx.x;
+  const int64_t b = plane / cout;
+  const int oc = static_cast<int>(plane - b * cout);
+  const int grp = oc / og, o = oc - grp * og;
+  const T* sp = src + ((b * g.groups + grp) * og + o) * static_cast<int64_t>(kvol) * in_vol;
+  if (sizeof(T) == 2 && (in_vol & 7) == 0 && (srow & 7) == 0 &&
+      (reinterpret_cast<uintptr_t>(sp) & 15u) == 0) {
+    // 16-byte copies (8 elements); srow keeps every staged row 16-byte aligned
+    const int vrow = in_vol / 8;
+    for (int e = threadIdx.x; e < kvol * vrow; e += blockDim.x) {
+      const int z = e / vrow, i = e - z * vrow;
+      *reinterpret_cast<uint4*>(sm + z * srow + i * 8) =
+          reinterpret_cast<const uint4*>(sp + static_cast<int64_t>(z) * in_vol)[i];
+    }
+  } else {
+    for (int z = 0; z < kvol; ++z)
+      for (int i = threadIdx.x; i < in_vol; i += blockDim.x) sm[z * srow + i] = sp[z * in_vol + i];
+  }
+  __syncthreads();
+  const float bv = bias != nullptr ? to_f32(bias[oc]) : 0.f;
+  T* dp = dst + plane * static_cast<int64_t>(rows) * d2;
+  const int lane = threadIdx.x & 31;
+  const int step_i = 32 / k2, step_z = 32 % k2;
+  for (int r = threadIdx.x >> 5; r < rows; r += blockDim.x >> 5) {
+    const int p1 = r % d1, p0 = r / d1;
+    const int i0 = p0 / k0, z0 = p0 - i0 * k0;
+    const int i1 = p1 / k1, z1 = p1 - i1 * k1;
+    const T* srow_p = sm + ((z0 * k1 + z1) * k2) * srow + (i0 * s1 + i1) * s2;
+    T* drow = dp + static_cast<int64_t>(r) * d2;
+    if (sizeof(T) == 2 && (d2 & 3) == 0 && (reinterpret_cast<uintptr_t>(drow) & 7u) == 0) {
+      // four consecutive outputs per lane, one 8-byte store
+      for (int X0 = lane * 4; X0 < d2; X0 += 128) {
+        int i2 = X0 / k2, z2 = X0 - (X0 / k2) * k2;
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[e] = to_f32(srow_p[z2 * srow + i2]);
+          if (bias != nullptr) v[e] += bv;
+          if (++z2 == k2) {
+            z2 = 0;
+            ++i2;
+          }
+        }
+        T o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = from_f32<T>(v[e]);
+        *reinterpret_cast<uint2*>(drow + X0) = *reinterpret_cast<const uint2*>(o);
+      }
+      continue;
+    }
+    int i2 = lane / k2, z2 = lane - (lane / k2) * k2;
+    for (int X = lane; X < d2; X += 32) {
+      float v = to_f32(srow_p[z2 * srow + i2]);
       if (bias != nullptr) v += bv;
       drow[X] = from_f32<T>(v);
       i2 += step_i;
@@ -209,6 +402,30 @@ int bio_im2col(int32_t dtype, const void* x, const bio_conv_geom* geom, void* pa
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bio::Geom g = to_geom(geom);
   const int64_t rows = geom->batch * geom->groups * L;
+  bool table = kpad <= bio::kIm2colTable && cg * geom->in[0] * geom->in[1] * geom->in[2] <
+                                                2147483647;
+  for (int i = 0; i < 3; ++i)
+    table = table && (geom->kernel[i] - 1) * geom->dilation[i] < 32767;
+  if (table) {
+    const int kr = static_cast<int>(k_real), kp = static_cast<int>(kpad);
+    switch (dtype) {
+      case BIO_F32:
+        bio::im2col_table_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(
+            static_cast<const float*>(x), static_cast<float*>(patches), g, kr, kp, rows);
+        break;
+      case BIO_F16:
+        bio::im2col_table_kernel<__half><<<blocks_for_rows(rows), 256, 0, s>>>(
+            static_cast<const __half*>(x), static_cast<__half*>(patches), g, kr, kp, rows);
+        break;
+      case BIO_BF16:
+        bio::im2col_table_kernel<__nv_bfloat16><<<blocks_for_rows(rows), 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(patches), g, kr,
+            kp, rows);
+        break;
+      default: return BIO_ERR_DTYPE;
+    }
+    return bio_host::launch_status(cudaGetLastError());
+  }
   switch (dtype) {
     case BIO_F32:
       bio::im2col_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(
@@ -242,6 +459,38 @@ int bio_depthwise_conv1d(int32_t dtype, const void* x, const void* w, const void
   if (st != BIO_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t rows = batch * channels;
+  {
+    const int64_t es = dtype == BIO_F32 ? 4 : 2;
+    const int64_t smem = 8 * lin * es;
+    if (smem <= 48 * 1024 && lout <= 2147483647 &&
+        (lout - 1) * static_cast<int64_t>(stride) + static_cast<int64_t>(ksize - 1) * dilation <
+            2147483647) {
+      const int li = static_cast<int>(lin), lo = static_cast<int>(lout);
+      switch (dtype) {
+        case BIO_F32:
+          bio::depthwise_conv1d_smem_kernel<float><<<blocks_for_rows(rows), 256, smem, s>>>(
+              static_cast<const float*>(x), static_cast<const float*>(w),
+              static_cast<const float*>(bias), static_cast<float*>(y), channels, li, lo, ksize,
+              stride, padding, dilation, rows);
+          break;
+        case BIO_F16:
+          bio::depthwise_conv1d_smem_kernel<__half><<<blocks_for_rows(rows), 256, smem, s>>>(
+              static_cast<const __half*>(x), static_cast<const __half*>(w),
+              static_cast<const __half*>(bias), static_cast<__half*>(y), channels, li, lo, ksize,
+              stride, padding, dilation, rows);
+          break;
+        case BIO_BF16:
+          bio::depthwise_conv1d_smem_kernel<__nv_bfloat16>
+              <<<blocks_for_rows(rows), 256, smem, s>>>(
+                  static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+                  static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
+                  channels, li, lo, ksize, stride, padding, dilation, rows);
+          break;
+        default: return BIO_ERR_DTYPE;
+      }
+      return bio_host::launch_status(cudaGetLastError());
+    }
+  }
   switch (dtype) {
     case BIO_F32:
       bio::depthwise_conv1d_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(
@@ -280,6 +529,44 @@ int bio_conv_transpose_scatter(int32_t dtype, const void* src, const void* bias,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bio::Geom g = to_geom(geom);
   const int64_t rows = total / (geom->in[2] * geom->kernel[2]);
+  {
+    // plane path: the plane's source rows fit in 48 KB of shared memory
+    const int64_t es = dtype == BIO_F32 ? 4 : 2;
+    const int64_t in_vol = geom->in[0] * geom->in[1] * geom->in[2];
+    const int64_t kvol = geom->kernel[0] * geom->kernel[1] * geom->kernel[2];
+    // row stride: 16-byte aligned and an odd multiple of 4 words for 2-byte
+    // types (k2 rows read by one warp fall in different banks), odd words
+    // for fp32
+    const int64_t srow = es == 2 ? ((in_vol + 7) / 8 * 8 + ((((in_vol + 7) / 8 * 8) / 8) % 2 == 0 ? 8 : 0))
+                                 : in_vol + 1;
+    const int64_t planes = geom->batch * geom->groups * out_channels_per_group;
+    const int64_t smem = kvol * srow * es;
+    if (smem <= 48 * 1024 && planes <= 2147483647 && out_vol <= 2147483647 &&
+        out_channels_per_group * geom->groups <= 2147483647) {
+      const unsigned grid = static_cast<unsigned>(planes);
+      const int og = static_cast<int>(out_channels_per_group);
+      const int sr = static_cast<int>(srow);
+      switch (dtype) {
+        case BIO_F32:
+          bio::convt_plane_kernel<float><<<grid, 256, smem, s>>>(
+              static_cast<const float*>(src), static_cast<const float*>(bias),
+              static_cast<float*>(dst), g, og, sr);
+          break;
+        case BIO_F16:
+          bio::convt_plane_kernel<__half><<<grid, 256, smem, s>>>(
+              static_cast<const __half*>(src), static_cast<const __half*>(bias),
+              static_cast<__half*>(dst), g, og, sr);
+          break;
+        case BIO_BF16:
+          bio::convt_plane_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(
+              static_cast<const __nv_bfloat16*>(src), static_cast<const __nv_bfloat16*>(bias),
+              static_cast<__nv_bfloat16*>(dst), g, og, sr);
+          break;
+        default: return BIO_ERR_DTYPE;
+      }
+      return bio_host::launch_status(cudaGetLastError());
+    }
+  }
   switch (dtype) {
     case BIO_F32:
       bio::convt_scatter_kernel<float><<<blocks_for_rows(rows), 256, 0, s>>>(

@@ -219,9 +219,9 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
 // tree are the same as in row_kernel, so results do not depend on which of the
 // two kernels a row length selects.
 template <typename TI, typename TO, bool LOG, int TEAM, int RMAX>
-__global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
+__global__ void __launch_bounds__(TEAM >= 128 ? TEAM : 256)
     row_softmax_reg_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t rows, int64_t n) {
-  constexpr int kTeamsPerBlock = TEAM >= 256 ? 1 : 256 / TEAM;
+  constexpr int kTeamsPerBlock = TEAM >= 128 ? 1 : 256 / TEAM;
   __shared__ float scratch[kTeamsPerBlock][TEAM / 32 + 1];
   const int team = threadIdx.x / TEAM;
   const int t = threadIdx.x % TEAM;
@@ -560,14 +560,24 @@ int launch_rows(const void* x, void* y, int64_t outer, int64_t n, int64_t inner,
     const int64_t cap = static_cast<int64_t>(sms) * 64;
     if (blocks > cap) blocks = cap;
     const unsigned g = static_cast<unsigned>(blocks);
-    if ((OP == bio::kSoftmax || OP == bio::kLogSoftmax) && team <= 256 && n <= team * 64) {
+    if ((OP == bio::kSoftmax || OP == bio::kLogSoftmax) && n <= 256 * 64) {
+      // register-resident rows: one warp (n <= 2048) or one 256-thread CTA
+      // per row; the team is a function of n
+      const int steam = n <= 2048 ? 32 : 256;
       constexpr bool kLog = OP == bio::kLogSoftmax;
-      const int64_t per = (n + 8 * team - 1) / (8 * team);  // groups per thread
+      const int64_t per = (n + 8 * steam - 1) / (8 * steam);  // groups per thread
       const int rmax = per <= 1 ? 1 : (per <= 2 ? 2 : (per <= 4 ? 4 : 8));
-#define BIO_REG_CASE(TM, R)                                                                  \
-  if (team == TM && rmax == R) {                                                             \
-    bio::row_softmax_reg_kernel<TI, TO, kLog, TM, R><<<g, 256, 0, stream>>>(xi, yo, outer, n); \
-    return bio_host::launch_status(cudaGetLastError());                                      \
+      const int threads = steam >= 128 ? steam : 256;
+      const int64_t rows_per_block = steam >= 128 ? 1 : 256 / steam;
+      int64_t sblocks = (outer + rows_per_block - 1) / rows_per_block;
+      const int64_t scap = static_cast<int64_t>(sms) * (2048 / threads) * 8;
+      if (sblocks > scap) sblocks = scap;
+      const unsigned sg = static_cast<unsigned>(sblocks);
+#define BIO_REG_CASE(TM, R)                                                                   \
+  if (steam == TM && rmax == R) {                                                             \
+    bio::row_softmax_reg_kernel<TI, TO, kLog, TM, R><<<sg, threads, 0, stream>>>(xi, yo, outer, \
+                                                                                 n);          \
+    return bio_host::launch_status(cudaGetLastError());                                       \
   }
       BIO_REG_CASE(32, 1)
       BIO_REG_CASE(32, 2)
