@@ -196,21 +196,47 @@ __global__ void __launch_bounds__(256)
     const int64_t c = bc % channels;
     const T* xr = x + bc * lin;
     __syncwarp();
+    if (sizeof(T) == 2 && (lin & 1) == 0) {
+      // 4-byte copies (rows of even length start 4-byte aligned)
+      const uint32_t* xw = reinterpret_cast<const uint32_t*>(xr);
+      uint32_t* sw = reinterpret_cast<uint32_t*>(srow);
 #pragma unroll 8
-    for (int i = lane; i < lin; i += 32) srow[i] = xr[i];
+      for (int i = lane; i < lin / 2; i += 32) sw[i] = xw[i];
+    } else {
+#pragma unroll 8
+      for (int i = lane; i < lin; i += 32) srow[i] = xr[i];
+    }
     __syncwarp();
     const T* wr = w + c * ksize;
     const float bv = bias != nullptr ? to_f32(bias[c]) : 0.f;
     T* yr = y + bc * lout;
-    for (int l = lane; l < lout; l += 32) {
-      float acc = 0.f;
-      const int i0 = l * stride - pad;
-      for (int k = 0; k < ksize; ++k) {
-        const int i = i0 + k * dil;
-        if (i >= 0 && i < lin) acc += to_f32(srow[i]) * to_f32(wr[k]);
+    if (ksize <= 8) {
+      float wk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) wk[k] = k < ksize ? to_f32(wr[k]) : 0.f;
+#pragma unroll 2
+      for (int l = lane; l < lout; l += 32) {
+        float acc = 0.f;
+        const int i0 = l * stride - pad;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int i = i0 + k * dil;
+          if (k < ksize && i >= 0 && i < lin) acc += to_f32(srow[i]) * wk[k];
+        }
+        if (bias != nullptr) acc += bv;
+        yr[l] = from_f32<T>(acc);
       }
-      if (bias != nullptr) acc += bv;
-      yr[l] = from_f32<T>(acc);
+    } else {
+      for (int l = lane; l < lout; l += 32) {
+        float acc = 0.f;
+        const int i0 = l * stride - pad;
+        for (int k = 0; k < ksize; ++k) {
+          const int i = i0 + k * dil;
+          if (i >= 0 && i < lin) acc += to_f32(srow[i]) * to_f32(wr[k]);
+        }
+        if (bias != nullptr) acc += bv;
+        yr[l] = from_f32<T>(acc);
+      }
     }
   }
 }

@@ -226,23 +226,34 @@ __global__ void __launch_bounds__(TEAM >= 128 ? TEAM : 256)
   const int team = threadIdx.x / TEAM;
   const int t = threadIdx.x % TEAM;
   const int64_t groups = (n + 7) / 8;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kTeamsPerBlock + team; r < rows;
-       r += static_cast<int64_t>(gridDim.x) * kTeamsPerBlock) {
+  // Rows are software-pipelined: the next row's groups are loaded into
+  // registers before the current row's reductions, so their latency overlaps
+  // the current row's work.
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kTeamsPerBlock;
+  auto load_row = [&](int64_t r, float (&v)[RMAX][8]) {
     const TI* row = x + r * n;
-    float v[RMAX][8];
-    float mx = -INFINITY;
 #pragma unroll
     for (int q = 0; q < RMAX; ++q) {
       const int64_t g = t + static_cast<int64_t>(q) * TEAM;
       if (g < groups) {
         load_group(row, g, n, v[q], -INFINITY);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[q][j]);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[q][j] = -INFINITY;
       }
     }
+  };
+  int64_t r = static_cast<int64_t>(blockIdx.x) * kTeamsPerBlock + team;
+  float v[RMAX][8];
+  if (r < rows) load_row(r, v);
+  for (; r < rows; r += stride) {
+    float nv[RMAX][8];
+    if (r + stride < rows) load_row(r + stride, nv);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[q][j]);
     mx = team_reduce<TEAM, true>(mx, scratch[team]);
     float den = 0.f;
 #pragma unroll
@@ -277,6 +288,10 @@ __global__ void __launch_bounds__(TEAM >= 128 ? TEAM : 256)
         store_group(out, g, n, o);
       }
     }
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q][j] = nv[q][j];
   }
 }
 
