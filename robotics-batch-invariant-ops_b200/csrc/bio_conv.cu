@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(256)
 // warp copies its (sample, channel) row with all loads in flight, then each
 // lane computes outputs from shared memory (same tap order k = 0..K-1 and
 // bias after the taps as depthwise_conv1d_kernel, so results are identical).
-template <typename T>
+template <typename T, int KS>
 __global__ void __launch_bounds__(256)
     depthwise_conv1d_smem_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                  const T* __restrict__ bias, T* __restrict__ y, int64_t channels,
@@ -210,18 +210,27 @@ __global__ void __launch_bounds__(256)
     const T* wr = w + c * ksize;
     const float bv = bias != nullptr ? to_f32(bias[c]) : 0.f;
     T* yr = y + bc * lout;
-    if (ksize <= 8) {
-      float wk[8];
+    if (KS > 0 && ksize == KS) {
+      constexpr int kTaps = KS > 0 ? KS : 1;
+      float wk[kTaps];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) wk[k] = k < ksize ? to_f32(wr[k]) : 0.f;
-#pragma unroll 2
+      for (int k = 0; k < kTaps; ++k) wk[k] = to_f32(wr[k]);
+      // outputs whose taps all lie inside the row need no bounds test
+      const int l_lo = pad > 0 ? (pad + stride - 1) / stride : 0;
+      const int l_hi_raw = (lin - 1 - (kTaps - 1) * dil + pad) / stride;  // last interior l
+      const int l_hi = (lin - 1 - (kTaps - 1) * dil + pad) < 0 ? -1 : l_hi_raw;
       for (int l = lane; l < lout; l += 32) {
         float acc = 0.f;
         const int i0 = l * stride - pad;
+        if (l >= l_lo && l <= l_hi) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int i = i0 + k * dil;
-          if (k < ksize && i >= 0 && i < lin) acc += to_f32(srow[i]) * wk[k];
+          for (int k = 0; k < kTaps; ++k) acc += to_f32(srow[i0 + k * dil]) * wk[k];
+        } else {
+#pragma unroll
+          for (int k = 0; k < kTaps; ++k) {
+            const int i = i0 + k * dil;
+            if (i >= 0 && i < lin) acc += to_f32(srow[i]) * wk[k];
+          }
         }
         if (bias != nullptr) acc += bv;
         yr[l] = from_f32<T>(acc);
@@ -411,6 +420,42 @@ bool geom_ok(const bio_conv_geom* c) {
 
 }  // namespace
 
+// Depthwise launch with the tap count as a template parameter for 2, 3 and
+// 4 taps (0 = any count).
+template <typename T>
+int launch_dw_smem(const void* x, const void* w, const void* bias, void* y, int64_t channels,
+                   int lin, int lout, int ksize, int stride, int pad, int dil, int64_t rows,
+                   int64_t smem, cudaStream_t s) {
+  const T* xt = static_cast<const T*>(x);
+  const T* wt = static_cast<const T*>(w);
+  const T* bt = static_cast<const T*>(bias);
+  T* yt = static_cast<T*>(y);
+  const unsigned g = blocks_for_rows(rows);
+  switch (ksize) {
+    case 2:
+      bio::depthwise_conv1d_smem_kernel<T, 2><<<g, 256, smem, s>>>(xt, wt, bt, yt, channels, lin,
+                                                                   lout, ksize, stride, pad, dil,
+                                                                   rows);
+      break;
+    case 3:
+      bio::depthwise_conv1d_smem_kernel<T, 3><<<g, 256, smem, s>>>(xt, wt, bt, yt, channels, lin,
+                                                                   lout, ksize, stride, pad, dil,
+                                                                   rows);
+      break;
+    case 4:
+      bio::depthwise_conv1d_smem_kernel<T, 4><<<g, 256, smem, s>>>(xt, wt, bt, yt, channels, lin,
+                                                                   lout, ksize, stride, pad, dil,
+                                                                   rows);
+      break;
+    default:
+      bio::depthwise_conv1d_smem_kernel<T, 0><<<g, 256, smem, s>>>(xt, wt, bt, yt, channels, lin,
+                                                                   lout, ksize, stride, pad, dil,
+                                                                   rows);
+      break;
+  }
+  return bio_host::launch_status(cudaGetLastError());
+}
+
 extern "C" {
 
 int bio_im2col(int32_t dtype, const void* x, const bio_conv_geom* geom, void* patches,
@@ -494,26 +539,20 @@ int bio_depthwise_conv1d(int32_t dtype, const void* x, const void* w, const void
       const int li = static_cast<int>(lin), lo = static_cast<int>(lout);
       switch (dtype) {
         case BIO_F32:
-          bio::depthwise_conv1d_smem_kernel<float><<<blocks_for_rows(rows), 256, smem, s>>>(
-              static_cast<const float*>(x), static_cast<const float*>(w),
-              static_cast<const float*>(bias), static_cast<float*>(y), channels, li, lo, ksize,
-              stride, padding, dilation, rows);
+          st = launch_dw_smem<float>(x, w, bias, y, channels, li, lo, ksize, stride, padding,
+                                     dilation, rows, smem, s);
           break;
         case BIO_F16:
-          bio::depthwise_conv1d_smem_kernel<__half><<<blocks_for_rows(rows), 256, smem, s>>>(
-              static_cast<const __half*>(x), static_cast<const __half*>(w),
-              static_cast<const __half*>(bias), static_cast<__half*>(y), channels, li, lo, ksize,
-              stride, padding, dilation, rows);
+          st = launch_dw_smem<__half>(x, w, bias, y, channels, li, lo, ksize, stride, padding,
+                                      dilation, rows, smem, s);
           break;
         case BIO_BF16:
-          bio::depthwise_conv1d_smem_kernel<__nv_bfloat16>
-              <<<blocks_for_rows(rows), 256, smem, s>>>(
-                  static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
-                  static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
-                  channels, li, lo, ksize, stride, padding, dilation, rows);
+          st = launch_dw_smem<__nv_bfloat16>(x, w, bias, y, channels, li, lo, ksize, stride,
+                                             padding, dilation, rows, smem, s);
           break;
         default: return BIO_ERR_DTYPE;
       }
+      if (st != BIO_OK) return st;
       return bio_host::launch_status(cudaGetLastError());
     }
   }

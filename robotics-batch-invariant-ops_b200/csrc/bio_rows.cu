@@ -295,6 +295,114 @@ __global__ void __launch_bounds__(TEAM >= 128 ? TEAM : 256)
   }
 }
 
+// Fast path of row_softmax_reg_kernel for rows made of whole, 16-byte
+// aligned groups (n % 8 == 0, aligned bases): no per-element bounds tests,
+// 32-bit indices, exponentials as ex2(x * log2e - max * log2e) with one FFMA.
+// Same element-to-thread assignment and reduction trees as the general
+// kernels; the next row is prefetched into registers before the current
+// row's reductions.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = to_f32(e[j]);
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&o)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    uint4 w;
+    T* e = reinterpret_cast<T*>(&w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) e[j] = from_f32<T>(o[j]);
+    *reinterpret_cast<uint4*>(p) = w;
+  } else {
+    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+__device__ __forceinline__ float ex2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename TI, typename TO, bool LOG, int TEAM, int RMAX>
+__global__ void __launch_bounds__(TEAM >= 128 ? TEAM : 256)
+    row_softmax_fast_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t rows, int n) {
+  constexpr int kTeamsPerBlock = TEAM >= 128 ? 1 : 256 / TEAM;
+  __shared__ float scratch[kTeamsPerBlock][TEAM / 32 + 1];
+  const int team = threadIdx.x / TEAM;
+  const int t = threadIdx.x % TEAM;
+  const int groups = n >> 3;
+  const float kLog2e = 1.4426950408889634f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kTeamsPerBlock;
+  auto load_row = [&](int64_t r, float (&v)[RMAX][8]) {
+    const TI* row = x + r * n;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q) {
+      const int g = t + q * TEAM;
+      if (g < groups) {
+        load8(row + g * 8, v[q]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q][j] = -INFINITY;
+      }
+    }
+  };
+  int64_t r = static_cast<int64_t>(blockIdx.x) * kTeamsPerBlock + team;
+  float v[RMAX][8];
+  if (r < rows) load_row(r, v);
+  for (; r < rows; r += stride) {
+    float nv[RMAX][8];
+    if (r + stride < rows) load_row(r + stride, nv);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[q][j]);
+    mx = team_reduce<TEAM, true>(mx, scratch[team]);
+    const float ml = (!LOG && mx == -INFINITY) ? 0.f : mx * kLog2e;
+    float den = 0.f;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float e = ex2f_approx(fmaf(v[q][j], kLog2e, -ml));
+        den += e;  // groups past the row end hold -inf: e = 0
+        if (!LOG) v[q][j] = e;
+      }
+    }
+    den = team_reduce<TEAM, false>(den, scratch[team]);
+    TO* out = y + r * n;
+    const float lse = LOG ? logf(den) : 0.f;
+    const float inv = den != 0.f ? 1.f / den : 0.f;
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q) {
+      const int g = t + q * TEAM;
+      if (g < groups) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = LOG ? (v[q][j] - mx - lse) : v[q][j] * inv;
+        store8(out + g * 8, o);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < RMAX; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q][j] = nv[q][j];
+  }
+}
+
 // Softmax / log-softmax of long rows (vocabulary-sized) by a cluster of CS
 // CTAs of kClusterTeam threads per row.  CTA c of the cluster owns the
 // contiguous groups [c*gpc, (c+1)*gpc) (gpc = ceil(groups / CS)) and keeps them
@@ -588,6 +696,25 @@ int launch_rows(const void* x, void* y, int64_t outer, int64_t n, int64_t inner,
       const int64_t scap = static_cast<int64_t>(sms) * (2048 / threads) * 8;
       if (sblocks > scap) sblocks = scap;
       const unsigned sg = static_cast<unsigned>(sblocks);
+      const bool fast = (n % 8) == 0 && n <= 2147483647 &&
+                        (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                        (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
+                        ((n * static_cast<int64_t>(sizeof(TI))) % 16) == 0 &&
+                        ((n * static_cast<int64_t>(sizeof(TO))) % 16) == 0;
+#define BIO_FAST_CASE(TM, R)                                                                   \
+  if (fast && steam == TM && rmax == R) {                                                      \
+    bio::row_softmax_fast_kernel<TI, TO, kLog, TM, R><<<sg, threads, 0, stream>>>(            \
+        xi, yo, outer, static_cast<int>(n));                                                   \
+    return bio_host::launch_status(cudaGetLastError());                                        \
+  }
+      BIO_FAST_CASE(32, 1)
+      BIO_FAST_CASE(32, 2)
+      BIO_FAST_CASE(32, 4)
+      BIO_FAST_CASE(32, 8)
+      BIO_FAST_CASE(256, 2)
+      BIO_FAST_CASE(256, 4)
+      BIO_FAST_CASE(256, 8)
+#undef BIO_FAST_CASE
 #define BIO_REG_CASE(TM, R)                                                                   \
   if (steam == TM && rmax == R) {                                                             \
     bio::row_softmax_reg_kernel<TI, TO, kLog, TM, R><<<sg, threads, 0, stream>>>(xi, yo, outer, \
