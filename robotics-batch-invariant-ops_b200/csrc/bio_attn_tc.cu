@@ -1101,24 +1101,35 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
         }
         tmem_st_wait();
       }
-      uint32_t f[4][32];
-      tmem_ld_32x32b_x32(s_addr + 0u, f[0]);
-      tmem_ld_32x32b_x32(s_addr + 32u, f[1]);
-      tmem_ld_32x32b_x32(s_addr + 64u, f[2]);
-      tmem_ld_32x32b_x32(s_addr + 96u, f[3]);
-      tmem_ld_wait();
+      // Scores stay in TMEM: pass 1 reads them two chunks at a time for the
+      // row maximum, pass 2 re-reads each chunk for the exponentials (the
+      // next chunk's load in flight while the current one is processed), so
+      // at most two 32-column chunks are held in registers.
       const uint32_t kNegInf = 0xff800000u;
-      if (plain && nvis < kAtBN) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
+      const bool clip = plain && nvis < kAtBN;  // plain rows: -inf past the visible range
+      auto clip_chunk = [&](uint32_t (&g)[32], int c) {
+        if (clip) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (c * 32 + j >= nvis) f[c][j] = kNegInf;
+            if (c * 32 + j >= nvis) g[j] = kNegInf;
+        }
+      };
+      float mx;
+      {
+        uint32_t g0[32], g1[32];
+        tmem_ld_32x32b_x32(s_addr + 0u, g0);
+        tmem_ld_32x32b_x32(s_addr + 32u, g1);
+        tmem_ld_wait();
+        clip_chunk(g0, 0);
+        clip_chunk(g1, 1);
+        mx = fmaxf(max32_words(g0), max32_words(g1));
+        tmem_ld_32x32b_x32(s_addr + 64u, g0);
+        tmem_ld_32x32b_x32(s_addr + 96u, g1);
+        tmem_ld_wait();
+        clip_chunk(g0, 2);
+        clip_chunk(g1, 3);
+        mx = fmax3(mx, max32_words(g0), max32_words(g1));
       }
-      const float mx = fmaxf(fmax3(max32_words(f[0]), max32_words(f[1]), max32_words(f[2])),
-                             max32_words(f[3]));
-      // Lazy reference point: m moves only when the block maximum exceeds it
-      // by more than 8 in log2 units (decided by this row's scores alone).
       const bool move = (m == -INFINITY) ? (mx != -INFINITY) : ((mx - m) * cexp > 8.f);
       const float m_new = move ? mx : m;
       const float alpha = (m == -INFINITY || !move) ? 1.f : ex2_approx((m - m_new) * cexp);
@@ -1143,8 +1154,15 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
       const float mc = (m_new == -INFINITY) ? 0.f : m_new * cexp;
       const uint64_t c2 = f2_pack(cexp, cexp), nmc2 = f2_pack(-mc, -mc);
       float lsum = 0.f;
+      uint32_t fa[32], fb[32];
+      tmem_ld_32x32b_x32(s_addr + 0u, fa);
+      tmem_ld_wait();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        uint32_t (&f)[32] = (c & 1) ? fb : fa;
+        uint32_t (&fn)[32] = (c & 1) ? fa : fb;
+        if (c + 1 < 4) tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>((c + 1) * 32), fn);
+        clip_chunk(f, c);
         uint64_t acc = f2_pack(0.f, 0.f);
         uint8_t* base = sPt + (c >> 1) * 16384 + r * 128;
 #pragma unroll
@@ -1154,8 +1172,8 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
           for (int e = 0; e < 4; ++e) {
             const int j = u4 * 8 + 2 * e;
             float a0, a1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(f[c][j]), __uint_as_float(f[c][j + 1])),
-                             c2, nmc2),
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(f[j]), __uint_as_float(f[j + 1])), c2,
+                             nmc2),
                       a0, a1);
 #if BIO_ATTN_EX2_F16X2
             // two exponentials per SFU operation on an fp16 pair
@@ -1178,6 +1196,7 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
         float s0, s1;
         f2_unpack(acc, s0, s1);
         lsum += s0 + s1;
+        if (c + 1 < 4) tmem_ld_wait();
       }
       if (m_new != -INFINITY) {
         l = l * alpha + lsum;
