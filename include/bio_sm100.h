@@ -268,7 +268,7 @@ typedef struct bio_attn_args {
   const void* cu_k;
   int32_t cu_is64;
   int64_t nseq;
-  void* workspace;     /* varlen, bf16/fp16: int32 [nseq + 1] scratch      */
+  void* workspace;     /* varlen, bf16/fp16: int32 [2 * nseq + 1] scratch  */
 } bio_attn_args;
 
 /* Dense SDPA over [batch][heads][lq|lk][d|dv].  Replaces
@@ -279,7 +279,7 @@ BIO_API int bio_attention(const bio_attn_args* args, void* stream);
  * (batch strides ignored); sequence s covers query tokens [cu_q[s], cu_q[s+1])
  * and keys [cu_k[s], cu_k[s+1]); query tokens outside every sequence are
  * written as zeros (bf16/fp16: the caller pre-zeroes o and passes an int32
- * [nseq + 1] workspace).  Offsets are read on the device (no host sync);
+ * [2 * nseq + 1] workspace).  Offsets are read on the device (no host sync);
  * invalid offsets raise BIO_DEV_INDEX and leave the affected rows zero.  Replaces
  * varlen_scaled_dot_product_attention_batch_invariant
  * (batch_invariant_ops.py:1216-1344). */

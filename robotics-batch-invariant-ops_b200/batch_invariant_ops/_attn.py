@@ -195,7 +195,7 @@ def varlen(q, k, v, cu_q, cu_k, *, is_causal, causal_name, scale):
     a.nseq = cu_q.numel() - 1
     workspace = None
     if half:
-        workspace = torch.empty(a.nseq + 1, dtype=torch.int32, device=q.device)
+        workspace = torch.empty(2 * a.nseq + 1, dtype=torch.int32, device=q.device)
         a.workspace = workspace.data_ptr()
     _lib.check(
         _lib.load().bio_attention_varlen(ctypes.byref(a), _lib.stream_of(q)), "bio_attention_varlen"

@@ -56,6 +56,7 @@ struct AttnTcParams {
   int cu_is64;
   int64_t nseq;
   const int* blk_start;
+  const int* order;  // two-tile varlen: planned position -> sequence id
   int* status;
 };
 
@@ -630,14 +631,37 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
   }
 }
 
+// Varlen plan (one thread): blk_start[i] = first q-block of the i-th planned
+// sequence, blk_start[nseq] = total.  With `order` (two-tile kernel) the
+// sequences are planned longest first (order[i] = sequence id, insertion sort
+// by q-block count for up to 4096 sequences, input order beyond) so that the
+// heaviest CTAs start first; without it the input order is kept.
 __global__ void attn_plan_kernel(const void* cu_q, int is64, int64_t nseq, int bm,
-                                 int* blk_start) {
+                                 int* blk_start, int* order) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int acc = 0;
-  for (int64_t s = 0; s < nseq; ++s) {
-    blk_start[s] = acc;
+  auto nblk = [&](int64_t s) -> int {
     const int64_t len = ld_off(cu_q, is64, s + 1) - ld_off(cu_q, is64, s);
-    if (len > 0) acc += static_cast<int>((len + bm - 1) / bm);
+    return len > 0 ? static_cast<int>((len + bm - 1) / bm) : 0;
+  };
+  if (order != nullptr) {
+    for (int64_t s = 0; s < nseq; ++s) order[s] = static_cast<int>(s);
+    if (nseq <= 4096) {
+      for (int64_t i = 1; i < nseq; ++i) {
+        const int v = order[i];
+        const int key = nblk(v);
+        int64_t j = i - 1;
+        while (j >= 0 && nblk(order[j]) < key) {
+          order[j + 1] = order[j];
+          --j;
+        }
+        order[j + 1] = v;
+      }
+    }
+  }
+  int acc = 0;
+  for (int64_t i = 0; i < nseq; ++i) {
+    blk_start[i] = acc;
+    acc += nblk(order != nullptr ? order[i] : i);
   }
   blk_start[nseq] = acc;
 }
@@ -832,9 +856,10 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
   const int lane = threadIdx.x & 31;
 
   // ---------------------------------------------------------------- work
-  int64_t b = 0, h = blockIdx.y, q0, lq_seq, lk_seq, q_tok0, k_tok0;
+  // grid (heads, q-blocks, batch): all heads of the heaviest q-blocks launch first
+  int64_t b = 0, h = blockIdx.x, q0, lq_seq, lk_seq, q_tok0, k_tok0;
   if (p.varlen) {
-    const int64_t g = blockIdx.x;
+    const int64_t g = blockIdx.y;
     const int64_t total = p.blk_start[p.nseq];
     if (g >= total) return;
     int64_t lo = 0, hi = p.nseq;
@@ -842,7 +867,8 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
       const int64_t mid = (lo + hi) >> 1;
       if (p.blk_start[mid] <= g) lo = mid; else hi = mid;
     }
-    const int64_t sq = lo;
+    const int64_t si = lo;
+    const int64_t sq = p.order[si];
     const int64_t qs0 = ld_off(p.cu_q, p.cu_is64, sq), qs1 = ld_off(p.cu_q, p.cu_is64, sq + 1);
     const int64_t ks0 = ld_off(p.cu_k, p.cu_is64, sq), ks1 = ld_off(p.cu_k, p.cu_is64, sq + 1);
     const bool bad = qs0 < 0 || qs1 > p.lq || ks0 < 0 || ks1 < ks0 || ks1 > p.lk ||
@@ -852,7 +878,8 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
       if (threadIdx.x == 0) raise_status(p.status, BIO_DEV_INDEX);
       return;  // output rows stay zero (pre-zeroed by the caller)
     }
-    q0 = (g - p.blk_start[sq]) * kAt2BM;
+    // latest q-block of the sequence first (heaviest under causal masking)
+    q0 = (p.blk_start[si + 1] - 1 - g) * kAt2BM;
     lq_seq = qs1 - qs0;
     lk_seq = ks1 - ks0;
     q_tok0 = qs0 + q0;
@@ -860,7 +887,7 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
   } else {
     b = blockIdx.z;
     // heaviest (latest, for causal) query blocks first
-    q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * kAt2BM;
+    q0 = static_cast<int64_t>(gridDim.y - 1 - blockIdx.y) * kAt2BM;
     lq_seq = p.lq;
     lk_seq = p.lk;
     q_tok0 = q0;
@@ -1364,12 +1391,12 @@ int launch_at2(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const 
   dim3 grid;
   if (varlen) {
     const int64_t g = (a->lq + bio::kAt2BM - 1) / bio::kAt2BM + a->nseq;
-    if (g > 2147483647) return BIO_ERR_SHAPE;
-    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads), 1);
+    if (g > 65535 || a->heads > 2147483647) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(a->heads), static_cast<unsigned>(g), 1);
   } else {
     const int64_t g = (a->lq + bio::kAt2BM - 1) / bio::kAt2BM;
-    if (g > 2147483647 || a->batch > 65535 || a->heads > 65535) return BIO_ERR_SHAPE;
-    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads),
+    if (g > 65535 || a->batch > 65535 || a->heads > 2147483647) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(a->heads), static_cast<unsigned>(g),
                 static_cast<unsigned>(a->batch));
   }
   kern<<<grid, bio::kAt2Threads, L::kTotal, s>>>(q, k, v, p);
@@ -1380,6 +1407,8 @@ int launch_at2(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const 
 // to work on (dense: more than 128 queries; varlen: always).
 bool use_two_tiles(int dp, int dvp, const bio_attn_args* a, bool varlen) {
   if (dp != dvp || (dp != 64 && dp != 128)) return false;
+  const int64_t qblocks = (a->lq + bio::kAt2BM - 1) / bio::kAt2BM + (varlen ? a->nseq : 0);
+  if (qblocks > 65535) return false;  // grid y holds the q-blocks
   return varlen || a->lq > bio::kAtBM;
 }
 
@@ -1458,13 +1487,16 @@ int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream) {
   p.cu_is64 = a->cu_is64;
   p.nseq = a->nseq;
   p.blk_start = static_cast<const int*>(a->workspace);
+  p.order = a->workspace != nullptr ? static_cast<const int*>(a->workspace) + a->nseq + 1
+                                    : nullptr;
   p.status = bio_host::status_word(a->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool two = use_two_tiles(dp, dvp, a, varlen);
   if (varlen) {
+    int* ws = static_cast<int*>(a->workspace);
     bio::attn_plan_kernel<<<1, 32, 0, s>>>(a->cu_q, a->cu_is64, a->nseq,
-                                           two ? bio::kAt2BM : bio::kAtBM,
-                                           static_cast<int*>(a->workspace));
+                                           two ? bio::kAt2BM : bio::kAtBM, ws,
+                                           two ? ws + a->nseq + 1 : nullptr);
     const int st = bio_host::launch_status(cudaGetLastError());
     if (st != BIO_OK) return st;
   }
