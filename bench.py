@@ -620,8 +620,14 @@ def _ops_cases(api, dev):
     logits = torch.randn(1024, 8, device=dev, generator=g)
     top, sel = torch.topk(logits, 2)
     rw = torch.softmax(top, -1)
-    cases.append(("moe T=1024 E=8 top-2 2048->5632 bf16 (dense, as the reference)",
+    sel64 = sel.contiguous()
+    cases.append(("moe T=1024 E=8 top-2 2048->5632 bf16 (routed rows only; flops of the routed "
+                  "rows)",
                   lambda: api.deterministic_token_choice_moe(hid, rw, sel, gw, uw, dw),
+                  6 * 1024 * 2 * 2048 * 5632, 2 * 3 * 8 * 2048 * 5632, None))
+    cases.append(("moe T=1024 E=8 top-2 2048->5632 bf16 (every expert on every token, the "
+                  "reference's schedule; same bits)",
+                  lambda: api.moe._dense_moe(hid, rw, sel64, gw, uw, dw),
                   6 * 1024 * 8 * 2048 * 5632, 2 * 3 * 8 * 2048 * 5632, None))
     # convolutions
     img = rn(32, 3, 224, 224)
@@ -695,6 +701,8 @@ def run_ops(args) -> None:
     peaks, _ = _peaks()
     rows = []
     for name, fn, fl, by, stock in _ops_cases(api, dev):
+        if args.ops_filter and args.ops_filter not in name:
+            continue
         try:
             t = _time_op(fn, flush)
         except Exception as exc:  # the reference may not support a case
@@ -775,6 +783,7 @@ def main() -> None:
     parser.add_argument("--triton-ref-worker", action="store_true", help=argparse.SUPPRESS)
     parser.add_argument("--profile-point", default=None, help="MxN: run one GEMM point (for ncu)")
     parser.add_argument("--ops", action="store_true", help="per-operator roofline table")
+    parser.add_argument("--ops-filter", default="", help="only --ops cases whose name has this")
     parser.add_argument("--ops-reference", action="store_true",
                         help="with --ops: time the reference package from baseline/_ref")
     args = parser.parse_args()

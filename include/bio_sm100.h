@@ -149,6 +149,18 @@ BIO_API int bio_gemm_f32_exact(const bio_gemm_args* args, void* workspace,
 BIO_API int bio_gemm_tiled(const bio_gemm_args* args, int32_t tile_m, int32_t tile_n,
                            void* stream);
 
+/* Segmented GEMM (f16/bf16 tensor-core path): segment s = 0..batch1-1 owns
+ * rows [seg[s], seg[s+1]) of A and C and multiplies them by B batch s
+ * (b + s * b_s1).  A and C are single matrices of m rows (a_s1 == c_s1 == 0,
+ * A K-contiguous), batch2 == 1, 1 <= batch1 <= 1024, k >= 1, no flags.  seg
+ * is a device int32 array [batch1 + 1] read on the device (no host sync);
+ * segments whose offsets are decreasing or outside [0, m] are skipped and
+ * raise BIO_DEV_INDEX; C rows outside every segment are not written.  Row r
+ * of a segment gets exactly the bits bio_gemm gives that row against the
+ * same B.  No counterpart in the reference (its experts run as one dense
+ * bmm over all tokens, moe.py:67-79). */
+BIO_API int bio_gemm_segmented(const bio_gemm_args* args, const int32_t* seg, void* stream);
+
 /* Copy a strided [nb1][nb2][rows][cols] operand into a dense
  * [nb1][nb2][rows][cols_pad] buffer (cols_pad >= cols, zero filled tail).
  * Used to bring odd strides into the 16-byte aligned K-contiguous layout the
@@ -305,6 +317,40 @@ BIO_API int bio_moe_route_sum(int32_t dtype, const void* expert_out, int32_t w_d
                               const void* routing_weights, const int64_t* selected_experts,
                               void* out, int64_t experts, int64_t tokens, int64_t top_k,
                               int64_t hidden, int32_t device, void* stream);
+
+/* Sparse MoE path: the same outputs as the dense path above, bit for bit,
+ * with each expert evaluated only on the tokens routed to it.
+ *
+ * bio_moe_plan sorts the slots (t, j) of selected_experts [tokens][top_k]
+ * by expert, stably (slot order within an expert), into an int32 workspace
+ * of at least bio_moe_plan_workspace(...) bytes laid out as
+ *   seg[experts + 1]       rows of expert e are [seg[e], seg[e+1])
+ *   slot_row[tokens*top_k] sorted row of slot t*top_k + j, -1 if invalid
+ *   row_token[tokens*top_k] token of sorted row r (r < seg[experts])
+ * followed by scratch.  Invalid expert ids raise BIO_DEV_INDEX and their
+ * slots get no row.  experts <= 1024.  Counting sort without atomic
+ * positions: the plan depends only on selected_experts.
+ *
+ * bio_moe_gather_rows writes x_sorted[r, :] = x[row_token[r], :] for the
+ * routed rows.  The expert GEMMs then run through bio_gemm_segmented with
+ * `seg` (segment e = expert e), followed by bio_silu_mul, and
+ * bio_moe_route_sum_sorted adds each token's routes left to right with the
+ * rounding of bio_moe_route_sum, reading route j from row slot_row[t*top_k+j].
+ * Every expert output row is computed by the same per-row arithmetic as in
+ * the dense path (the GEMM result of a row never depends on the other rows),
+ * so the two paths agree exactly.  No counterpart in the reference, which
+ * evaluates every expert on every token (moe.py:67-92). */
+BIO_API int64_t bio_moe_plan_workspace(int64_t experts, int64_t tokens, int64_t top_k);
+BIO_API int bio_moe_plan(const int64_t* selected_experts, int64_t experts, int64_t tokens,
+                         int64_t top_k, void* workspace, int64_t workspace_bytes,
+                         int32_t device, void* stream);
+BIO_API int bio_moe_gather_rows(int32_t dtype, const void* x, int64_t hidden, const void* plan,
+                                int64_t experts, int64_t tokens, int64_t top_k,
+                                void* x_sorted, int32_t device, void* stream);
+BIO_API int bio_moe_route_sum_sorted(int32_t dtype, const void* y_sorted, int32_t w_dtype,
+                                     const void* routing_weights, const void* plan, void* out,
+                                     int64_t experts, int64_t tokens, int64_t top_k,
+                                     int64_t hidden, int32_t device, void* stream);
 
 /* ---- convolution that allocates nothing ---------------------------------
  * No counterpart in the reference (its convolutions allocate their im2col

@@ -259,6 +259,29 @@ def moe(hidden, routing_weights, selected_experts, gate_w, up_w, down_w):
     return out
 
 
+def moe_route_plan(selected_experts, experts):
+    """Expected plan of the sparse MoE path: slots t*top_k + j sorted by
+    expert, stably.  Returns (seg [E+1], slot_row [S] with -1 for ids outside
+    [0, E), row_token [seg[E]]) as int64 tensors.  The dense evaluation that
+    the sparse path must reproduce is moe.py:67-92 (``moe`` above)."""
+    sel = selected_experts.detach().cpu().long().reshape(-1)
+    top_k = selected_experts.shape[1] if selected_experts.ndim == 2 else 1
+    valid = (sel >= 0) & (sel < experts)
+    counts = torch.bincount(sel[valid], minlength=experts)
+    seg = torch.zeros(experts + 1, dtype=torch.int64)
+    seg[1:] = torch.cumsum(counts, 0)
+    slot_row = torch.full_like(sel, -1)
+    row_token = torch.zeros(int(seg[-1]), dtype=torch.int64)
+    nxt = seg[:-1].clone()
+    for i in range(sel.numel()):  # sequential: stable by construction
+        e = int(sel[i])
+        if 0 <= e < experts:
+            slot_row[i] = nxt[e]
+            row_token[nxt[e]] = i // top_k
+            nxt[e] += 1
+    return seg, slot_row, row_token
+
+
 def topk_routing(logits, k):
     """Top-k expert choice with lowest-index tie-break and a softmax over the
     selected logits (the caller-side router of the MoE configs)."""

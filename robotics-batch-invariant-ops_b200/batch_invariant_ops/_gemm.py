@@ -191,8 +191,13 @@ def launch(
     alpha: float = 1.0,
     tile: tuple[int, int] | None = None,
     exact_f32: bool = True,
+    segments: torch.Tensor | None = None,
 ) -> None:
     """Enqueue one GEMM on the current stream of ``c``'s device.
+
+    ``segments`` (device int32 [batch1 + 1] row offsets) selects
+    bio_gemm_segmented: segment s owns rows [segments[s], segments[s+1]) of A
+    and C and multiplies them by B batch s.
 
     fp32 runs on the int8 tensor cores with exact integer slices
     (bio_gemm_f32_exact, workspace from the caching allocator) whenever that
@@ -228,6 +233,14 @@ def launch(
     args.alpha = alpha
     args.device = c.device.index
     lib = _lib.load()
+    if segments is not None:
+        _lib.check(
+            lib.bio_gemm_segmented(
+                ctypes.byref(args), ctypes.c_void_p(segments.data_ptr()), _lib.stream_of(c)
+            ),
+            "bio_gemm_segmented",
+        )
+        return
     if tile is None and c.dtype == torch.float32 and exact_f32:
         ws_bytes = lib.bio_gemm_f32_exact_workspace(ctypes.byref(args))
         if ws_bytes > 0:

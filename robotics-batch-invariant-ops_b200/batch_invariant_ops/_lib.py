@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "bio_gemm_tiled": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _I32, _I32, _P]),
     "bio_gemm_f32_exact_workspace": (_I64, [ctypes.POINTER(GemmArgs)]),
     "bio_gemm_f32_exact": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _I64, _P]),
+    "bio_gemm_segmented": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _P]),
     "bio_softmax": (ctypes.c_int, [_I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "bio_reduce": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "bio_im2col": (ctypes.c_int, [_I32, _P, _P, _P, _I64, _I32, _P]),
@@ -104,6 +105,13 @@ SIGNATURES: dict[str, tuple] = {
     "bio_attention_varlen": (ctypes.c_int, [_P, _P]),
     "bio_silu_mul": (ctypes.c_int, [_I32, _P, _P, _P, _I64, _I32, _P]),
     "bio_moe_route_sum": (
+        ctypes.c_int,
+        [_I32, _P, _I32, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
+    ),
+    "bio_moe_plan_workspace": (_I64, [_I64, _I64, _I64]),
+    "bio_moe_plan": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _I64, _I32, _P]),
+    "bio_moe_gather_rows": (ctypes.c_int, [_I32, _P, _I64, _P, _I64, _I64, _I64, _P, _I32, _P]),
+    "bio_moe_route_sum_sorted": (
         ctypes.c_int,
         [_I32, _P, _I32, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     ),

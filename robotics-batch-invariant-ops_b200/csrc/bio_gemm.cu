@@ -39,6 +39,12 @@ struct TcGemmParams {
   // single-CTA kernel: k-blocks moved per tensor copy (1, or 2/4/8 with the
   // K-chunked 5-D maps); the ring is grouped in runs of kchunk slots
   int kchunk;
+  // segmented GEMM (seg != nullptr): segment s owns A/C rows
+  // [seg[s], seg[s+1]) and B batch s; nseg segments, batch2 == 1.  Every CTA
+  // builds a table of m-tiles per segment at start, so tiles are only ever
+  // issued for rows that exist and the tile count needs no host sync.
+  const int* seg;
+  int nseg;
   int64_t batch2;
   int64_t total_tiles;
   int a_div2, b_div2;
@@ -78,6 +84,91 @@ __device__ __forceinline__ TileIdx decode_tile(int64_t t, int tiles_m, int tiles
   ti.b1 = bi / batch2;
   ti.b2 = bi - ti.b1 * batch2;
   return ti;
+}
+
+// Segmented GEMMs: at most kMaxSegs segments.  Each CTA keeps the offsets
+// and an exclusive prefix of m-tiles per segment in shared memory.
+constexpr int kMaxSegs = 1024;
+constexpr uint32_t kSegBytes = 2 * (kMaxSegs + 1) * 4;
+
+struct TileSeg {
+  int base, rows;  // first A/C row of the tile's segment and its row count
+};
+
+// Build the segment table (one warp).  A segment whose offsets are out of
+// order or outside [0, m] gets no tiles and raises BIO_DEV_INDEX.
+__device__ __forceinline__ void seg_table_build(const TcGemmParams& p, int tile_m, int* seg_off,
+                                                int* seg_tiles, int lane) {
+  const int ns = p.nseg;
+  const int per = (ns + 31) / 32;
+  const int s0 = min(lane * per, ns);
+  const int s1 = min(s0 + per, ns);
+  int sum = 0;
+  bool bad = false;
+  for (int s = s0; s < s1; ++s) {
+    const int lo = p.seg[s];
+    const int hi = p.seg[s + 1];
+    const bool ok = lo >= 0 && lo <= hi && hi <= p.m;
+    bad |= !ok;
+    const int cnt = ok ? (hi - lo + tile_m - 1) / tile_m : 0;
+    seg_off[s] = lo;
+    seg_tiles[s] = cnt;
+    sum += cnt;
+  }
+  if (lane == 0) seg_off[ns] = p.seg[ns];
+  int incl = sum;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  int run = incl - sum;
+  for (int s = s0; s < s1; ++s) {
+    const int cnt = seg_tiles[s];
+    seg_tiles[s] = run;
+    run += cnt;
+  }
+  if (lane == 31) seg_tiles[ns] = incl;
+  if (__any_sync(0xffffffffu, bad) && lane == 0) raise_status(p.status, BIO_DEV_INDEX);
+}
+
+// Tiles of the launch: the host count, or (segmented) m-tiles x n-tiles from
+// the shared table.
+__device__ __forceinline__ int64_t tile_total(const TcGemmParams& p, const int* seg_tiles) {
+  return p.seg != nullptr ? static_cast<int64_t>(seg_tiles[p.nseg]) * p.tiles_n : p.total_tiles;
+}
+
+// Tile t -> indices and its segment.  Segmented: the raster runs over the
+// concatenated m-tiles of all segments; a binary search over the prefix
+// finds the segment (empty segments have equal prefix entries and are
+// never chosen) and the m-block within it.
+__device__ __forceinline__ TileIdx tile_at(int64_t t, const TcGemmParams& p, const int* seg_off,
+                                           const int* seg_tiles, TileSeg* sg) {
+  if (p.seg == nullptr) {
+    sg->base = 0;
+    sg->rows = p.m;
+    return decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+  }
+  TileIdx ti = decode_tile(t, seg_tiles[p.nseg], p.tiles_n, 1, p.group_m);
+  int lo = 0, hi = p.nseg;  // seg_tiles[lo] <= mb < seg_tiles[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (seg_tiles[mid] <= ti.mb)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  ti.mb -= seg_tiles[lo];
+  ti.b1 = lo;
+  sg->base = seg_off[lo];
+  sg->rows = seg_off[lo + 1] - seg_off[lo];
+  return ti;
+}
+
+// Rows of a segment slab: any row makes the whole 128-row slab load (rows
+// past the segment only feed outputs that are not stored).
+__device__ __forceinline__ int seg_valid(const TcGemmParams& p, int v) {
+  return (p.seg != nullptr && v > 0 && v < 128) ? 128 : v;
 }
 
 template <typename T>
@@ -128,7 +219,7 @@ struct TcSmem {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kData = STAGES * kStageBytes;
   static constexpr uint32_t kBarBytes = (2 * kMaxStages1 + 5) * 8 + 16;
-  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes;
+  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes + kSegBytes;
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
@@ -159,6 +250,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* seg_off = reinterpret_cast<int*>(smem + L::kData + L::kBarBytes);
+  int* seg_tiles = seg_off + kMaxSegs + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -189,10 +282,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
+  if (p.seg != nullptr && warp == 2) seg_table_build(p, kBM, seg_off, seg_tiles, lane);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int64_t total = tile_total(p, seg_tiles);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -201,13 +296,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int64_t issued = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
-        const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+      for (int64_t t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        TileSeg sg;
+        const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
         const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
         const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
         const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
         const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
-        const int valid = p.m - ti.mb * kBM;
+        const int valid = seg_valid(p, sg.rows - ti.mb * kBM);
+        const int arow = sg.base + ti.mb * kBM;
         const uint32_t a_bytes = A_MN ? L::kABytes : a_slab_bytes(valid, p.a_tail_rows);
         for (int kb = 0; kb < k_groups; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
@@ -221,17 +318,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (kc > 1) {
             // kc consecutive k-blocks of A and B, one copy each; the smem
             // image equals kc consecutive single-block slots
-            tma_load_5d(a_dst, &tmA5, &full_bar[stage], 0, ti.mb * kBM, kb * kc, a2, a1);
+            tma_load_5d(a_dst, &tmA5, &full_bar[stage], 0, arow, kb * kc, a2, a1);
             tma_load_5d(b_dst, &tmB5, &full_bar[stage], 0, ti.nb * BN, kb * kc, b2, b1);
           } else if constexpr (!A_MN) {
             if (valid >= kBM)
-              tma_load_4d(a_dst, &tmA, &full_bar[stage], kb * kBK, ti.mb * kBM, a2, a1);
+              tma_load_4d(a_dst, &tmA, &full_bar[stage], kb * kBK, arow, a2, a1);
             else
-              tma_load_4d(a_dst, &tmA_tail, &full_bar[stage], kb * kBK, ti.mb * kBM, a2, a1);
+              tma_load_4d(a_dst, &tmA_tail, &full_bar[stage], kb * kBK, arow, a2, a1);
           } else {
 #pragma unroll
             for (int j = 0; j < kBM / 64; ++j) {
-              tma_load_4d(a_dst + j * kBoxBytesMN, &tmA, &full_bar[stage], ti.mb * kBM + j * 64,
+              tma_load_4d(a_dst + j * kBoxBytesMN, &tmA, &full_bar[stage], arow + j * 64,
                           kb * kBK, a2, a1);
             }
           }
@@ -274,7 +371,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      for (int64_t t = blockIdx.x; ok && t < total; t += gridDim.x) {
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -318,14 +415,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const T* bias = static_cast<const T*>(p.bias);
-    for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
-      const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+      TileSeg sg;
+      const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const int m = ti.mb * kBM + q * 32 + lane;
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
-                static_cast<int64_t>(m) * p.c_sm;
+                static_cast<int64_t>(sg.base + m) * p.c_sm;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -334,7 +432,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            r);
         tmem_ld_wait();
         const int n0 = ti.nb * BN + c0;
-        if (m < p.m && n0 < p.n) {
+        if (m < sg.rows && n0 < p.n) {
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
@@ -411,7 +509,7 @@ struct Tc2Smem {
   static constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
   static constexpr uint32_t kData = STAGES * (kABytes + kBBytes);
   static constexpr uint32_t kBarBytes = (2 * kMaxStages2 + 5) * 8 + 16;
-  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes;
+  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes + kSegBytes;
 };
 
 // Bounded spin on the global timer (used only on the abort path so that copies
@@ -447,6 +545,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* seg_off = reinterpret_cast<int*>(smem + L::kData + L::kBarBytes);
+  int* seg_tiles = seg_off + kMaxSegs + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -476,11 +576,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tmem_alloc_2sm(tmem_slot, kTmemCols);
     tmem_relinquish_2sm();
   }
+  if (p.seg != nullptr && warp == 2) seg_table_build(p, 256, seg_off, seg_tiles, lane);
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int64_t total = tile_total(p, seg_tiles);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -488,19 +590,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int64_t t = pair; ok && t < p.total_tiles; t += npairs) {
-        const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+      for (int64_t t = pair; ok && t < total; t += npairs) {
+        TileSeg sg;
+        const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
         const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
         const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
         const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
         const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
-        const int a_row = ti.mb * 256 + static_cast<int>(rank) * 128;
+        const int a_row = sg.base + ti.mb * 256 + static_cast<int>(rank) * 128;
         const int b_row = ti.nb * BN + static_cast<int>(rank) * BNH;
-        const int valid0 = p.m - ti.mb * 256;
-        const int my_valid = valid0 - static_cast<int>(rank) * 128;
+        const int valid0 = sg.rows - ti.mb * 256;
+        const int my_valid = seg_valid(p, valid0 - static_cast<int>(rank) * 128);
         // A_MN operands always move full boxes (zero-filled past M)
-        const uint32_t a0 = A_MN ? L::kABytes : a_slab_bytes(valid0, p.a_tail_rows);
-        const uint32_t a1b = A_MN ? L::kABytes : a_slab_bytes(valid0 - 128, p.a_tail_rows);
+        const uint32_t a0 = A_MN ? L::kABytes : a_slab_bytes(seg_valid(p, valid0), p.a_tail_rows);
+        const uint32_t a1b =
+            A_MN ? L::kABytes : a_slab_bytes(seg_valid(p, valid0 - 128), p.a_tail_rows);
         const uint32_t tx = a0 + a1b + 2 * L::kBBytes;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
@@ -543,7 +647,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int64_t t = pair; ok && t < p.total_tiles; t += npairs) {
+      for (int64_t t = pair; ok && t < total; t += npairs) {
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -583,14 +687,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const T* bias = static_cast<const T*>(p.bias);
-    for (int64_t t = pair; t < p.total_tiles; t += npairs) {
-      const TileIdx ti = decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+    for (int64_t t = pair; t < total; t += npairs) {
+      TileSeg sg;
+      const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
-                static_cast<int64_t>(m) * p.c_sm;
+                static_cast<int64_t>(sg.base + m) * p.c_sm;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -599,7 +704,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
                            r);
         tmem_ld_wait();
         const int n0 = ti.nb * BN + c0;
-        if (m < p.m && n0 < p.n) {
+        if (m < sg.rows && n0 < p.n) {
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
@@ -983,7 +1088,7 @@ int group_rows(int64_t k, int bm, int tiles_m) {
 }
 
 template <bool PAIR, int BN, bool A_MN, bool B_MN, typename T>
-int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
+int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream) {
   constexpr int STAGES = stages_for<PAIR, BN>();
   constexpr uint32_t kSmem = smem_bytes<PAIR, BN, STAGES>();
   constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
@@ -1077,7 +1182,7 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   if constexpr (PAIR) {
     // M <= 128: no CTA ever holds a full 128-row slab, so the A stages can be
     // packed at the tail-box stride and the freed space buys more stages.
-    if (!A_MN && a->m <= 128) {
+    if (!A_MN && a->m <= 128 && seg == nullptr) {
       using L2 = bio::Tc2Smem<BN, STAGES>;
       const int stride = tail_rows > 0 ? tail_rows * kBK * 2 : 128 * kBK * 2;
       int st_n = static_cast<int>(L2::kData / static_cast<uint32_t>(stride + L2::kBBytes));
@@ -1092,7 +1197,7 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   } else {
     // Single CTA, M <= 128: one m-block whose A slab is packed at the
     // tail-box stride; the freed space holds more B stages.
-    if (!A_MN && a->m <= 128 && tail_rows > 0) {
+    if (!A_MN && a->m <= 128 && tail_rows > 0 && seg == nullptr) {
       using L1 = bio::TcSmem<BN, STAGES>;
       const int stride = tail_rows * kBK * 2;
       int st_n = static_cast<int>(L1::kData / static_cast<uint32_t>(stride + L1::kBBytes));
@@ -1112,7 +1217,7 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   p.kchunk = 1;
   CUtensorMap tmA5 = tmA, tmB5 = tmB;
   if constexpr (!PAIR && !A_MN && !B_MN) {
-    if (a->m <= 128 && a->k % 64 == 0) {
+    if (a->m <= 128 && a->k % 64 == 0 && seg == nullptr) {
       using L1 = bio::TcSmem<BN, STAGES>;
       const int target = static_cast<int>((32u * 1024u) / L1::kBBytes);  // ~32 KB of B per copy
       for (int c = 8; c >= 2; c >>= 1) {
@@ -1133,6 +1238,13 @@ int launch_tc(const bio_gemm_args* a, cudaStream_t stream) {
   }
   p.batch2 = a->batch2;
   p.total_tiles = batch * p.tiles_m * p.tiles_n;
+  p.seg = seg;
+  p.nseg = static_cast<int>(a->batch1);
+  if (seg != nullptr) {
+    // upper bound: a segment of r rows has at most r / kTileM + 1 m-tiles
+    p.total_tiles = (a->m / kTileM + a->batch1) * p.tiles_n;
+    p.group_m = group_rows(a->k, kTileM, static_cast<int>(a->m / kTileM + a->batch1));
+  }
   p.a_div2 = static_cast<int>(a->a_div2);
   p.b_div2 = static_cast<int>(a->b_div2);
   p.a_bcast1 = a_b1;
@@ -1173,28 +1285,29 @@ bool tile_supported(const TileChoice& tc) {
 }
 
 template <bool A_MN, bool B_MN, typename T>
-int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream) {
+int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, const int* seg,
+                cudaStream_t stream) {
   if (tc.pair) {
-    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, stream);
-    return launch_tc<true, 256, A_MN, B_MN, T>(a, stream);
+    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, seg, stream);
+    return launch_tc<true, 256, A_MN, B_MN, T>(a, seg, stream);
   }
   switch (tc.bn) {
-    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, stream);
-    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, stream);
-    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, stream);
-    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, stream);
+    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream);
+    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream);
+    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream);
+    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream);
   }
 }
 
 template <typename T>
 int dispatch_tc(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream, bool a_mn,
-                bool b_mn) {
+                bool b_mn, const int* seg = nullptr) {
   if (a_mn) {
-    return b_mn ? dispatch_bn<true, true, T>(a, tc, stream)
-                : dispatch_bn<true, false, T>(a, tc, stream);
+    return b_mn ? dispatch_bn<true, true, T>(a, tc, seg, stream)
+                : dispatch_bn<true, false, T>(a, tc, seg, stream);
   }
-  return b_mn ? dispatch_bn<false, true, T>(a, tc, stream)
-              : dispatch_bn<false, false, T>(a, tc, stream);
+  return b_mn ? dispatch_bn<false, true, T>(a, tc, seg, stream)
+              : dispatch_bn<false, false, T>(a, tc, seg, stream);
 }
 
 int launch_f32(const bio_gemm_args* a, cudaStream_t stream) {
@@ -1335,6 +1448,40 @@ int bio_gemm_tiled(const bio_gemm_args* a, int32_t tile_m, int32_t tile_n, void*
   const TileChoice tc{tile_m == 256, static_cast<int>(tile_n)};
   if (!tile_supported(tc)) return BIO_ERR_ARG;
   return gemm_impl(a, &tc, stream_v);
+}
+
+int bio_gemm_segmented(const bio_gemm_args* a, const int32_t* seg, void* stream_v) {
+  if (a == nullptr || seg == nullptr) return BIO_ERR_ARG;
+  if (a->flags != 0 || a->a_div2 < 1 || a->b_div2 < 1) return BIO_ERR_ARG;
+  if (a->dtype != BIO_F16 && a->dtype != BIO_BF16) return BIO_ERR_DTYPE;
+  if (a->batch2 != 1 || a->batch1 < 1 || a->batch1 > bio::kMaxSegs) return BIO_ERR_SHAPE;
+  if (a->m < 0 || a->n < 0 || a->k < 1) return BIO_ERR_SHAPE;
+  if (a->m > 2147483647 || a->n > 2147483647 || a->k > 2147483647) return BIO_ERR_SHAPE;
+  if (a->m == 0 || a->n == 0) return BIO_OK;
+  // one A and one C matrix whose rows the segments share; A rows start at
+  // arbitrary offsets, so A must be K-contiguous (a row index is never the
+  // innermost tensor-map coordinate)
+  if (a->a_s1 != 0 || a->c_s1 != 0 || a->a_sk != 1) return BIO_ERR_STRIDE;
+  if (a->a == nullptr || a->b == nullptr || a->c == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(a->device);
+  if (st != BIO_OK) return st;
+  if (!aligned16(a->a) || !aligned16(a->b)) return BIO_ERR_ALIGN;
+  bool b_mn;
+  if (a->b_sk == 1) {
+    b_mn = false;
+  } else if (a->b_sn == 1) {
+    b_mn = true;
+  } else {
+    return BIO_ERR_STRIDE;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  // tile from the mean rows per segment (the counts live on the device); any
+  // tile gives the same bits
+  TileChoice tc = pick_tile((a->m + a->batch1 - 1) / a->batch1, a->n, a->batch1,
+                            bio_host::sm_count(a->device));
+  if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
+  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, false, b_mn, seg);
+  return dispatch_tc<__half>(a, tc, stream, false, b_mn, seg);
 }
 
 int bio_pack_rows(int32_t dtype, const void* src, int64_t nb1, int64_t nb2, int64_t rows,
