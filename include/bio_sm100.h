@@ -181,7 +181,8 @@ BIO_API int bio_pack_rows(int32_t dtype, const void* src, int64_t nb1, int64_t n
 
 /* Softmax / log-softmax over n.  Softmax keeps the reference's edge rules:
  * a row whose maximum is -inf, or whose denominator is 0, produces zeros.
- * Log-softmax requires dtype_out == dtype_in.  Output has the input's shape.
+ * Log-softmax requires dtype_out == dtype_in or BIO_F32 (half_to_float).
+ * Output has the input's shape.
  * Replaces _softmax_kernel / softmax (batch_invariant_ops.py:1075-1145) and
  * _log_softmax_kernel / log_softmax (batch_invariant_ops.py:975-1071). */
 BIO_API int bio_softmax(int32_t dtype_in, int32_t dtype_out, const void* x, void* y,

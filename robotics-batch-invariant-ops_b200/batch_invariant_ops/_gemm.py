@@ -268,8 +268,9 @@ def mm(
     bias: torch.Tensor | None = None,
     tile: tuple[int, int] | None = None,
     exact_f32: bool = True,
+    alpha: float = 1.0,
 ) -> torch.Tensor:
-    """C[M,N] = A[M,K] @ B[K,N] (+ bias[N]); any strides.  ``tile`` forces an
+    """C[M,N] = alpha * A[M,K] @ B[K,N] (+ bias[N]); any strides.  ``tile`` forces an
     output tile (tests of tile independence); ``exact_f32=False`` runs fp32 on
     the fp64-accumulating kernel instead of the exact-slice tensor-core path."""
     m, k = a.shape
@@ -286,7 +287,7 @@ def mm(
         opb = operand_b(b, 1, 1, k, n, b.stride(0), b.stride(1), 0, 0)
     launch(
         opa, opb, c, batch1=1, batch2=1, m=m, n=n, k=k, c_sm=n, c_sn=1, c_s1=0, c_s2=0, bias=bias,
-        tile=tile, exact_f32=exact_f32,
+        tile=tile, exact_f32=exact_f32, alpha=alpha,
     )
     return c
 

@@ -99,8 +99,26 @@ def mm_batch_invariant(a, b):
     return matmul_persistent(a, b)
 
 
-def addmm_batch_invariant(bias, a, b):
-    return matmul_persistent(a, b, bias=bias)
+def addmm_batch_invariant(bias, a, b, *, beta=1, alpha=1):
+    """``aten::addmm``: beta * bias + alpha * (a @ b) (reference :1604-1605,
+    which takes only the default beta = alpha = 1).  alpha scales the fp32
+    accumulator before the bias add; beta * bias is formed in fp32 and
+    rounded to the bias dtype once per column, the same for every row, so
+    the result stays batch invariant.  beta = 0 ignores bias (as aten does)."""
+    if beta == 1 and alpha == 1:
+        return matmul_persistent(a, b, bias=bias)
+    assert a.shape[1] == b.shape[0], "Incompatible dimensions"
+    assert a.dtype == b.dtype, "Incompatible dtypes"
+    assert (
+        bias is None or bias.dim() == 1
+    ), "Currently assuming bias is 1D, let Horace know if you run into this"
+    assert a.dtype in _FLOAT_TYPES, f"unsupported dtype: {a.dtype}"
+    _require_cuda(a, b, bias)
+    if beta == 0:
+        bias = None
+    elif beta != 1 and bias is not None:
+        bias = (bias.float() * float(beta)).to(bias.dtype)
+    return _gemm.mm(a, b, bias, alpha=float(alpha))
 
 
 def linear_batch_invariant(input, weight, bias=None):
@@ -220,13 +238,29 @@ def softmax(
     return _rows.softmax(input, dim, dtype, log=False)
 
 
+def _half_to_float_input(input):
+    assert input.dtype in {torch.float16, torch.bfloat16}, (
+        "half_to_float requires a float16 or bfloat16 input"
+    )
+
+
 def _log_softmax_batch_invariant(input, dim, _half_to_float):
-    assert not _half_to_float, "not implemented"
+    """``aten::_log_softmax``; half_to_float (a 16-bit input with an fp32
+    result, which the reference rejects, :1623-1625) stores the same fp32
+    row result without the final rounding to 16 bits."""
+    if _half_to_float:
+        _half_to_float_input(input)
+        _require_cuda(input)
+        return _rows.softmax(input, dim, torch.float32, log=True)
     return log_softmax(input, dim=dim)
 
 
 def _softmax_batch_invariant(input, dim, _half_to_float):
-    assert not _half_to_float, "not implemented"
+    """``aten::_softmax``; half_to_float as for _log_softmax (reference
+    :1628-1630 rejects it)."""
+    if _half_to_float:
+        _half_to_float_input(input)
+        return softmax(input, dim=dim, dtype=torch.float32)
     return softmax(input, dim=dim)
 
 

@@ -802,7 +802,8 @@ int bio_softmax(int32_t dtype_in, int32_t dtype_out, const void* x, void* y, int
   const int sms = bio_host::sm_count(device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (log_softmax) {
-    if (dtype_out != dtype_in) return BIO_ERR_DTYPE;
+    // same dtype, or fp32 out (aten::_log_softmax with half_to_float)
+    if (dtype_out != dtype_in && dtype_out != BIO_F32) return BIO_ERR_DTYPE;
     return dispatch<bio::kLogSoftmax>(dtype_in, dtype_out, x, y, outer, n, inner, s, sms);
   }
   return dispatch<bio::kSoftmax>(dtype_in, dtype_out, x, y, outer, n, inner, s, sms);

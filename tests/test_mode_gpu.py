@@ -111,3 +111,32 @@ def test_mode_context_is_exception_safe_and_reentrant():
             assert is_batch_invariant_mode_enabled()
             raise RuntimeError("sentinel")
     assert not is_batch_invariant_mode_enabled()
+
+
+def test_mode_addmm_beta_alpha():
+    gen = torch.Generator(device="cuda").manual_seed(7311)
+    x = torch.randn(9, 300, device="cuda", generator=gen).to(torch.bfloat16)
+    w = torch.randn(300, 70, device="cuda", generator=gen).to(torch.bfloat16)
+    b = torch.randn(70, device="cuda", generator=gen).to(torch.bfloat16)
+    ref = torch.addmm(b.float(), x.float(), w.float(), beta=0.5, alpha=2.0)
+    with set_batch_invariant_mode():
+        full = torch.addmm(b, x, w, beta=0.5, alpha=2.0)
+        assert_first_sample_equal(torch.addmm(b, x[:1], w, beta=0.5, alpha=2.0), full)
+        no_bias = torch.addmm(b, x, w, beta=0, alpha=1.5)
+    torch.testing.assert_close(full.float(), ref, **TOLERANCES[torch.bfloat16])
+    torch.testing.assert_close(no_bias.float(), 1.5 * (x.float() @ w.float()),
+                               **TOLERANCES[torch.bfloat16])
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+@pytest.mark.parametrize("op", (torch.ops.aten._softmax, torch.ops.aten._log_softmax))
+def test_mode_softmax_half_to_float(dtype, op):
+    gen = torch.Generator(device="cuda").manual_seed(7312)
+    x = (torch.randn(6, 5, 1000, device="cuda", generator=gen) * 3).to(dtype)
+    ref = op(x.float(), -1, False)
+    with set_batch_invariant_mode():
+        full = op(x, -1, True)
+        alone = op(x[:1], -1, True)
+    assert full.dtype == torch.float32
+    assert_first_sample_equal(alone, full)
+    torch.testing.assert_close(full, ref, rtol=1e-5, atol=1e-6)
