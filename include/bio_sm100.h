@@ -161,6 +161,19 @@ BIO_API int bio_gemm_tiled(const bio_gemm_args* args, int32_t tile_m, int32_t ti
  * bmm over all tokens, moe.py:67-79). */
 BIO_API int bio_gemm_segmented(const bio_gemm_args* args, const int32_t* seg, void* stream);
 
+/* Fused SwiGLU expert GEMM (f16/bf16): C = silu(A·gateᵀ) * (A·upᵀ) with the
+ * roundings of two bio_gemm calls followed by bio_silu_mul (gate and up
+ * rounded to the dtype, silu rounded, product rounded), bit for bit.  `args`
+ * describes the gate GEMM (b = gate weights, n = output columns, no bias, no
+ * flags); `up` has the same dims and strides as b.  One CTA pair computes a
+ * 256-row tile of gate and up for 128 output columns in one 256-wide
+ * accumulator (the leader loads gate rows, its peer the same up rows), so A
+ * is read once and the gate/up outputs never reach HBM.  `seg` (optional)
+ * selects the segmented mode of bio_gemm_segmented.  No counterpart in the
+ * reference (moe.py:75-79 runs gate, up and silu*up as separate ops). */
+BIO_API int bio_gemm_swiglu(const bio_gemm_args* args, const void* up, const int32_t* seg,
+                            void* stream);
+
 /* Copy a strided [nb1][nb2][rows][cols] operand into a dense
  * [nb1][nb2][rows][cols_pad] buffer (cols_pad >= cols, zero filled tail).
  * Used to bring odd strides into the 16-byte aligned K-contiguous layout the

@@ -192,12 +192,15 @@ def launch(
     tile: tuple[int, int] | None = None,
     exact_f32: bool = True,
     segments: torch.Tensor | None = None,
+    swiglu_up: Operand | None = None,
 ) -> None:
     """Enqueue one GEMM on the current stream of ``c``'s device.
 
     ``segments`` (device int32 [batch1 + 1] row offsets) selects
     bio_gemm_segmented: segment s owns rows [segments[s], segments[s+1]) of A
-    and C and multiplies them by B batch s.
+    and C and multiplies them by B batch s.  ``swiglu_up`` (an operand with
+    the same layout as ``b``) selects bio_gemm_swiglu: C = silu(A·B) * (A·up)
+    with the roundings of separate GEMMs and bio_silu_mul.
 
     fp32 runs on the int8 tensor cores with exact integer slices
     (bio_gemm_f32_exact, workspace from the caching allocator) whenever that
@@ -233,6 +236,20 @@ def launch(
     args.alpha = alpha
     args.device = c.device.index
     lib = _lib.load()
+    if swiglu_up is not None:
+        if (swiglu_up.s_row, swiglu_up.s_col, swiglu_up.s1, swiglu_up.s2) != (
+            b.s_row, b.s_col, b.s1, b.s2
+        ):
+            raise ValueError("swiglu up operand must share the gate operand's layout")
+        _lib.check(
+            lib.bio_gemm_swiglu(
+                ctypes.byref(args), ctypes.c_void_p(swiglu_up.ptr),
+                ctypes.c_void_p(segments.data_ptr() if segments is not None else None),
+                _lib.stream_of(c),
+            ),
+            "bio_gemm_swiglu",
+        )
+        return
     if segments is not None:
         _lib.check(
             lib.bio_gemm_segmented(

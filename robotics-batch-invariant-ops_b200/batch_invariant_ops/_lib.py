@@ -93,6 +93,7 @@ SIGNATURES: dict[str, tuple] = {
     "bio_gemm_f32_exact_workspace": (_I64, [ctypes.POINTER(GemmArgs)]),
     "bio_gemm_f32_exact": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _I64, _P]),
     "bio_gemm_segmented": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _P]),
+    "bio_gemm_swiglu": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _P, _P]),
     "bio_softmax": (ctypes.c_int, [_I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "bio_reduce": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "bio_im2col": (ctypes.c_int, [_I32, _P, _P, _P, _I64, _I32, _P]),

@@ -71,13 +71,53 @@ def _route_weights(routing_weights: torch.Tensor) -> torch.Tensor:
     return weights
 
 
+def _swiglu_operands(x, gate_weight, up_weight, rows, x_batch, x_s1):
+    """(A, gate B, up B) operands for bio_gemm_swiglu, or None when the two
+    weights do not end up with one layout (the separate path then runs)."""
+    e, n, k = gate_weight.shape
+    opa = _gemm.operand_a(x, e, 1, rows, k, x.stride(-2), x.stride(-1), x_s1, 0)
+    opg = _gemm.operand_b(gate_weight, e, 1, k, n, gate_weight.stride(2), gate_weight.stride(1),
+                          gate_weight.stride(0), 0)
+    opu = _gemm.operand_b(up_weight, e, 1, k, n, up_weight.stride(2), up_weight.stride(1),
+                          up_weight.stride(0), 0)
+    if (opg.s_row, opg.s_col, opg.s1, opg.s2) != (opu.s_row, opu.s_col, opu.s1, opu.s2):
+        return None
+    return opa, opg, opu
+
+
+def _fused_gate_up(x, gate_weight, up_weight, segments=None):
+    """act = silu(x @ gate^T) * (x @ up^T) per expert in one fused GEMM
+    (bio_gemm_swiglu), bit-identical to the separate GEMMs + bio_silu_mul.
+    Dense: x [T, K] broadcast to every expert, act [E, T, N].  Segmented:
+    x [S, K] in expert order, act [S, N].  None when not applicable."""
+    e, n, k = gate_weight.shape
+    if x.dtype not in (torch.float16, torch.bfloat16) or k == 0 or n == 0:
+        return None
+    rows = x.shape[0]
+    ops = _swiglu_operands(x, gate_weight, up_weight, rows, e, 0)
+    if ops is None:
+        return None
+    opa, opg, opu = ops
+    if segments is None:
+        act = torch.empty((e, rows, n), device=x.device, dtype=x.dtype)
+        c_s1 = rows * n
+    else:
+        act = torch.empty((rows, n), device=x.device, dtype=x.dtype)
+        c_s1 = 0
+    if act.numel() == 0:
+        return act
+    _gemm.launch(opa, opg, act, batch1=e, batch2=1, m=rows, n=n, k=k, c_sm=n, c_sn=1,
+                 c_s1=c_s1, c_s2=0, segments=segments, swiglu_up=opu)
+    return act
+
+
 def _dense_moe(h, routing_weights, sel, gate_weight, up_weight, down_weight) -> torch.Tensor:
     """Every expert on every token (the reference's schedule)."""
     num_experts, _, hidden_size = gate_weight.shape
     token_count, top_k = sel.shape
-    gate = _expert_bmm(h, gate_weight, 0)
-    up = _expert_bmm(h, up_weight, 0)
-    act = _silu_mul(gate, up)
+    act = _fused_gate_up(h, gate_weight, up_weight)
+    if act is None:
+        act = _silu_mul(_expert_bmm(h, gate_weight, 0), _expert_bmm(h, up_weight, 0))
     expert_out = _expert_bmm(act, down_weight, act.stride(0))
     weights = _route_weights(routing_weights)
     out = torch.empty((token_count, hidden_size), device=h.device, dtype=h.dtype)
@@ -139,7 +179,9 @@ def _sparse_moe(h, routing_weights, sel, gate_weight, up_weight, down_weight) ->
         "bio_moe_gather_rows",
     )
     seg = plan[: num_experts + 1]
-    act = _silu_mul(_segmented_mm(xs, gate_weight, seg), _segmented_mm(xs, up_weight, seg))
+    act = _fused_gate_up(xs, gate_weight, up_weight, seg)
+    if act is None:
+        act = _silu_mul(_segmented_mm(xs, gate_weight, seg), _segmented_mm(xs, up_weight, seg))
     ys = _segmented_mm(act, down_weight, seg)
     weights = _route_weights(routing_weights)
     out = torch.empty((token_count, hidden_size), device=h.device, dtype=h.dtype)

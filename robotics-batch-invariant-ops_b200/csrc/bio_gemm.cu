@@ -45,6 +45,11 @@ struct TcGemmParams {
   // issued for rows that exist and the tile count needs no host sync.
   const int* seg;
   int nseg;
+  // SwiGLU mode (CTA pair, BN = 256): the leader CTA's half of the B tile
+  // comes from tmB (gate) and the peer's from tmB2 (up) at the same rows, so
+  // accumulator columns [0, 128) hold gate and [128, 256) up for 128 output
+  // columns; the epilogue stores round(silu(round(gate)) * round(up)).
+  int swiglu;
   int64_t batch2;
   int64_t total_tiles;
   int a_div2, b_div2;
@@ -524,7 +529,8 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmA_tail, const TcGemmParams p) {
+                    const __grid_constant__ CUtensorMap tmA_tail,
+                    const __grid_constant__ CUtensorMap tmB2, const TcGemmParams p) {
   using L = Tc2Smem<BN, STAGES>;
   constexpr int BNH = BN / 2;
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -570,7 +576,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(p.swiglu && rank == 1 ? &tmB2 : &tmB);
   }
   if (warp == 1) {
     tmem_alloc_2sm(tmem_slot, kTmemCols);
@@ -598,7 +604,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
         const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
         const int a_row = sg.base + ti.mb * 256 + static_cast<int>(rank) * 128;
-        const int b_row = ti.nb * BN + static_cast<int>(rank) * BNH;
+        const int b_row = p.swiglu ? ti.nb * BNH : ti.nb * BN + static_cast<int>(rank) * BNH;
+        const CUtensorMap* mapB = (p.swiglu && rank == 1) ? &tmB2 : &tmB;
         const int valid0 = sg.rows - ti.mb * 256;
         const int my_valid = seg_valid(p, valid0 - static_cast<int>(rank) * 128);
         // A_MN operands always move full boxes (zero-filled past M)
@@ -626,11 +633,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
               tma_load_4d_2sm(a_dst + j * kBoxBytesMN, &tmA, bar, a_row + j * 64, kb * kBK, a2, a1);
           }
           if constexpr (!B_MN) {
-            tma_load_4d_2sm(b_dst, &tmB, bar, kb * kBK, b_row, b2, b1);
+            tma_load_4d_2sm(b_dst, mapB, bar, kb * kBK, b_row, b2, b1);
           } else {
 #pragma unroll
             for (int j = 0; j < BNH / 64; ++j)
-              tma_load_4d_2sm(b_dst + j * kBoxBytesMN, &tmB, bar, b_row + j * 64, kb * kBK, b2, b1);
+              tma_load_4d_2sm(b_dst + j * kBoxBytesMN, mapB, bar, b_row + j * 64, kb * kBK, b2, b1);
           }
           if (++stage == nstages) {
             stage = 0;
@@ -696,6 +703,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
                 static_cast<int64_t>(sg.base + m) * p.c_sm;
+      if (p.swiglu) {
+        // gate in accumulator columns [0, BNH), up in [BNH, BN); the
+        // roundings of separate gate / up GEMMs followed by bio_silu_mul
+#pragma unroll 1
+        for (int c0 = 0; c0 < BNH; c0 += 32) {
+          uint32_t rg[32], ru[32];
+          const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+          tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) + lanes, rg);
+          tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + BNH + c0) + lanes, ru);
+          tmem_ld_wait();
+          const int n0 = ti.nb * BNH + c0;
+          if (m < sg.rows && n0 < p.n) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float g = round_to<T>(__uint_as_float(rg[j]) * p.alpha);
+              const float u = round_to<T>(__uint_as_float(ru[j]) * p.alpha);
+              v[j] = round_to<T>(g / (1.f + expf(-g))) * u;
+            }
+            if (p.c_vec_ok && n0 + 32 <= p.n) {
+              uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 w;
+                w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+                w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+                w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+                w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+                dst[j] = w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -1088,7 +1139,8 @@ int group_rows(int64_t k, int bm, int tiles_m) {
 }
 
 template <bool PAIR, int BN, bool A_MN, bool B_MN, typename T>
-int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream) {
+int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
+              const void* b_up = nullptr) {
   constexpr int STAGES = stages_for<PAIR, BN>();
   constexpr uint32_t kSmem = smem_bytes<PAIR, BN, STAGES>();
   constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
@@ -1167,13 +1219,24 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream) {
   st = B_MN ? encode_map(&tmB, a->dtype, a->b, mb, 64, kBK)
             : encode_map(&tmB, a->dtype, a->b, mb, kBK, kBoxBRows);
   if (st != BIO_OK) return st;
+  // SwiGLU: the up weights share the gate weights' dims and strides
+  CUtensorMap tmB2 = tmB;
+  if (b_up != nullptr) {
+    if (!PAIR || BN != 256) return BIO_ERR_ARG;
+    st = B_MN ? encode_map(&tmB2, a->dtype, b_up, mb, 64, kBK)
+              : encode_map(&tmB2, a->dtype, b_up, mb, kBK, kBoxBRows);
+    if (st != BIO_OK) return st;
+  }
 
   bio::TcGemmParams p;
   p.m = static_cast<int>(a->m);
   p.n = static_cast<int>(a->n);
   p.k = static_cast<int>(a->k);
   p.tiles_m = static_cast<int>((a->m + kTileM - 1) / kTileM);
-  p.tiles_n = static_cast<int>((a->n + BN - 1) / BN);
+  // SwiGLU tiles produce BN / 2 output columns (gate and up halves)
+  const int out_bn = b_up != nullptr ? BN / 2 : BN;
+  p.tiles_n = static_cast<int>((a->n + out_bn - 1) / out_bn);
+  p.swiglu = b_up != nullptr ? 1 : 0;
   p.k_blocks = static_cast<int>((a->k + kBK - 1) / kBK);
   p.group_m = group_rows(a->k, kTileM, p.tiles_m);
   p.a_tail_rows = tail_rows;
@@ -1271,7 +1334,8 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream) {
   const int64_t n_units = p.total_tiles < units ? p.total_tiles : units;
   const int64_t grid = PAIR ? 2 * n_units : n_units;
   if constexpr (PAIR)
-    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail, p);
+    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
+                                                                          tmB2, p);
   else
     kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
                                                                           tmA5, tmB5, p);
@@ -1437,6 +1501,70 @@ int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v) 
   return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn);
 }
 
+template <typename T>
+int dispatch_swiglu(const bio_gemm_args* a, const int* seg, const void* up, cudaStream_t stream,
+                    bool a_mn, bool b_mn) {
+  if (a_mn)
+    return b_mn ? launch_tc<true, 256, true, true, T>(a, seg, stream, up)
+                : launch_tc<true, 256, true, false, T>(a, seg, stream, up);
+  return b_mn ? launch_tc<true, 256, false, true, T>(a, seg, stream, up)
+              : launch_tc<true, 256, false, false, T>(a, seg, stream, up);
+}
+
+// Shared body of bio_gemm_segmented (seg != null) and bio_gemm_swiglu (up !=
+// null; seg optional).
+int grouped_impl(const bio_gemm_args* a, const int32_t* seg, const void* up, void* stream_v) {
+  if (a == nullptr) return BIO_ERR_ARG;
+  if (a->flags != 0 || a->a_div2 < 1 || a->b_div2 < 1) return BIO_ERR_ARG;
+  if (up != nullptr && a->bias != nullptr) return BIO_ERR_ARG;
+  if (a->dtype != BIO_F16 && a->dtype != BIO_BF16) return BIO_ERR_DTYPE;
+  if (a->m < 0 || a->n < 0 || a->k < 1 || a->batch1 < 1 || a->batch2 < 1) return BIO_ERR_SHAPE;
+  if (a->m > 2147483647 || a->n > 2147483647 || a->k > 2147483647) return BIO_ERR_SHAPE;
+  if (a->batch1 > 2147483647 || a->batch2 > 2147483647) return BIO_ERR_SHAPE;
+  if (seg != nullptr) {
+    if (a->batch2 != 1 || a->batch1 > bio::kMaxSegs) return BIO_ERR_SHAPE;
+    // one A and one C matrix whose rows the segments share; A rows start at
+    // arbitrary offsets, so A must be K-contiguous (a row index is never the
+    // innermost tensor-map coordinate)
+    if (a->a_s1 != 0 || a->c_s1 != 0 || a->a_sk != 1) return BIO_ERR_STRIDE;
+  }
+  if (a->m == 0 || a->n == 0) return BIO_OK;
+  if (a->a == nullptr || a->b == nullptr || a->c == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(a->device);
+  if (st != BIO_OK) return st;
+  if (!aligned16(a->a) || !aligned16(a->b) || (up != nullptr && !aligned16(up)))
+    return BIO_ERR_ALIGN;
+  bool a_mn;
+  if (a->a_sk == 1) {
+    a_mn = false;
+  } else if (a->a_sm == 1) {
+    a_mn = true;
+  } else {
+    return BIO_ERR_STRIDE;
+  }
+  bool b_mn;
+  if (a->b_sk == 1) {
+    b_mn = false;
+  } else if (a->b_sn == 1) {
+    b_mn = true;
+  } else {
+    return BIO_ERR_STRIDE;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (up != nullptr) {
+    if (a->dtype == BIO_BF16)
+      return dispatch_swiglu<__nv_bfloat16>(a, seg, up, stream, a_mn, b_mn);
+    return dispatch_swiglu<__half>(a, seg, up, stream, a_mn, b_mn);
+  }
+  // tile from the mean rows per segment (the counts live on the device); any
+  // tile gives the same bits
+  TileChoice tc = pick_tile((a->m + a->batch1 - 1) / a->batch1, a->n, a->batch1,
+                            bio_host::sm_count(a->device));
+  if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
+  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn, seg);
+  return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn, seg);
+}
+
 }  // namespace
 
 extern "C" {
@@ -1451,37 +1579,14 @@ int bio_gemm_tiled(const bio_gemm_args* a, int32_t tile_m, int32_t tile_n, void*
 }
 
 int bio_gemm_segmented(const bio_gemm_args* a, const int32_t* seg, void* stream_v) {
-  if (a == nullptr || seg == nullptr) return BIO_ERR_ARG;
-  if (a->flags != 0 || a->a_div2 < 1 || a->b_div2 < 1) return BIO_ERR_ARG;
-  if (a->dtype != BIO_F16 && a->dtype != BIO_BF16) return BIO_ERR_DTYPE;
-  if (a->batch2 != 1 || a->batch1 < 1 || a->batch1 > bio::kMaxSegs) return BIO_ERR_SHAPE;
-  if (a->m < 0 || a->n < 0 || a->k < 1) return BIO_ERR_SHAPE;
-  if (a->m > 2147483647 || a->n > 2147483647 || a->k > 2147483647) return BIO_ERR_SHAPE;
-  if (a->m == 0 || a->n == 0) return BIO_OK;
-  // one A and one C matrix whose rows the segments share; A rows start at
-  // arbitrary offsets, so A must be K-contiguous (a row index is never the
-  // innermost tensor-map coordinate)
-  if (a->a_s1 != 0 || a->c_s1 != 0 || a->a_sk != 1) return BIO_ERR_STRIDE;
-  if (a->a == nullptr || a->b == nullptr || a->c == nullptr) return BIO_ERR_ARG;
-  int st = bio_host::ensure_device(a->device);
-  if (st != BIO_OK) return st;
-  if (!aligned16(a->a) || !aligned16(a->b)) return BIO_ERR_ALIGN;
-  bool b_mn;
-  if (a->b_sk == 1) {
-    b_mn = false;
-  } else if (a->b_sn == 1) {
-    b_mn = true;
-  } else {
-    return BIO_ERR_STRIDE;
-  }
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  // tile from the mean rows per segment (the counts live on the device); any
-  // tile gives the same bits
-  TileChoice tc = pick_tile((a->m + a->batch1 - 1) / a->batch1, a->n, a->batch1,
-                            bio_host::sm_count(a->device));
-  if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
-  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, false, b_mn, seg);
-  return dispatch_tc<__half>(a, tc, stream, false, b_mn, seg);
+  if (seg == nullptr) return BIO_ERR_ARG;
+  return grouped_impl(a, seg, nullptr, stream_v);
+}
+
+int bio_gemm_swiglu(const bio_gemm_args* a, const void* up, const int32_t* seg,
+                    void* stream_v) {
+  if (up == nullptr) return BIO_ERR_ARG;
+  return grouped_impl(a, seg, up, stream_v);
 }
 
 int bio_pack_rows(int32_t dtype, const void* src, int64_t nb1, int64_t nb2, int64_t rows,

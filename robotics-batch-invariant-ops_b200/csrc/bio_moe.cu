@@ -26,6 +26,26 @@ __global__ void silu_mul_kernel(const T* __restrict__ gate, const T* __restrict_
   }
 }
 
+// Same arithmetic, 16 bytes of elements per thread (aligned, n % V == 0).
+template <typename T>
+__global__ void silu_mul_vec_kernel(const T* __restrict__ gate, const T* __restrict__ up,
+                                    T* __restrict__ out, int64_t nvec) {
+  constexpr int V = 16 / sizeof(T);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nvec;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    T g[V], u[V], o[V];
+    *reinterpret_cast<uint4*>(g) = reinterpret_cast<const uint4*>(gate)[i];
+    *reinterpret_cast<uint4*>(u) = reinterpret_cast<const uint4*>(up)[i];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float x = to_f32(g[j]);
+      const float sv = round_to<T>(x / (1.f + expf(-x)));
+      o[j] = from_f32<T>(sv * to_f32(u[j]));
+    }
+    reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
 template <typename T, typename WT>
 __global__ void route_sum_kernel(const T* __restrict__ y, const WT* __restrict__ w,
                                  const int64_t* __restrict__ sel, T* __restrict__ out,
@@ -59,7 +79,7 @@ __global__ void route_sum_kernel(const T* __restrict__ y, const WT* __restrict__
 // Route plan: the slots (t, j) of a [tokens, top_k] selection sorted by
 // expert, stably (ascending slot index within an expert), by a counting sort
 // with no atomics on positions:
-//   1. count: block b histograms its kPlanChunk slots per expert (shared
+//   1. count: block b histograms its kPlanChunk (256) slots per expert (shared
 //      atomics: counts do not depend on their order)
 //   2. scan:  per expert, exclusive prefix over blocks, then over experts ->
 //      seg[e] and each (block, expert) start position
@@ -68,7 +88,7 @@ __global__ void route_sum_kernel(const T* __restrict__ y, const WT* __restrict__
 // Outputs (int32): seg[E + 1] (rows of expert e: [seg[e], seg[e+1])),
 // slot_row[S] (sorted row of slot i, -1 for an invalid expert id) and
 // row_token[S] (token of sorted row r; rows >= seg[E] unused).
-constexpr int kPlanChunk = 1024;
+constexpr int kPlanChunk = 256;
 
 __global__ void moe_count_kernel(const int64_t* __restrict__ sel, int64_t slots, int experts,
                                  int* __restrict__ blockcnt, int* status) {
@@ -452,6 +472,31 @@ int bio_silu_mul(int32_t dtype, const void* gate, const void* up, void* out, int
   int st = bio_host::ensure_device(device);
   if (st != BIO_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
+                         reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+  const int64_t per = dtype == BIO_F32 ? 4 : 8;
+  if (aligned && n % per == 0 && (dtype == BIO_F32 || dtype == BIO_F16 || dtype == BIO_BF16)) {
+    const int64_t nvec = n / per;
+    const unsigned g = grid_for(nvec);
+    switch (dtype) {
+      case BIO_F32:
+        bio::silu_mul_vec_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(gate),
+                                                          static_cast<const float*>(up),
+                                                          static_cast<float*>(out), nvec);
+        break;
+      case BIO_F16:
+        bio::silu_mul_vec_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(gate),
+                                                           static_cast<const __half*>(up),
+                                                           static_cast<__half*>(out), nvec);
+        break;
+      default:
+        bio::silu_mul_vec_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up),
+            static_cast<__nv_bfloat16*>(out), nvec);
+        break;
+    }
+    return bio_host::launch_status(cudaGetLastError());
+  }
   switch (dtype) {
     case BIO_F32:
       bio::silu_mul_kernel<float><<<grid_for(n), 256, 0, s>>>(

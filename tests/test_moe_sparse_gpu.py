@@ -178,3 +178,52 @@ def test_sparse_moe_out_of_range_expert_zeroes_row():
     dense = moe_mod._dense_moe(h, w, sel, gate, gate, down)
     _lib.clear_device_status()
     assert torch.equal(out, dense)
+
+
+@pytest.mark.parametrize("dtype", HALF)
+@pytest.mark.parametrize("t,e,n,k", [(1, 2, 80, 64), (37, 3, 200, 136), (300, 4, 5632, 512),
+                                     (129, 2, 128, 2048), (1024, 1, 384, 1000)])
+def test_fused_swiglu_gemm_equals_separate_gemms_and_silu(dtype, t, e, n, k):
+    gen = torch.Generator(device="cuda").manual_seed(t * 7 + n + k)
+    x = _rn(t, k, dtype=dtype, gen=gen)
+    gate = _rn(e, n, k, dtype=dtype, gen=gen, scale=k**-0.5)
+    up = _rn(e, n, k, dtype=dtype, gen=gen, scale=k**-0.5)
+    fused = moe_mod._fused_gate_up(x, gate, up)
+    assert fused is not None and fused.shape == (e, t, n)
+    separate = moe_mod._silu_mul(moe_mod._expert_bmm(x, gate, 0), moe_mod._expert_bmm(x, up, 0))
+    assert torch.equal(fused, separate)
+    # segmented: rows split unevenly over the experts (one segment empty)
+    cuts = sorted({0, t} | {int(v) for v in torch.randint(0, t + 1, (e - 1,), generator=torch.Generator().manual_seed(t)).tolist()})
+    while len(cuts) < e + 1:
+        cuts.insert(1, 0)
+    seg = torch.tensor(cuts, dtype=torch.int32, device="cuda")
+    fused_seg = moe_mod._fused_gate_up(x, gate, up, seg)
+    sep_seg = moe_mod._silu_mul(moe_mod._segmented_mm(x, gate, seg), moe_mod._segmented_mm(x, up, seg))
+    for s in range(e):
+        lo, hi = cuts[s], cuts[s + 1]
+        assert torch.equal(fused_seg[lo:hi], sep_seg[lo:hi]), s
+        assert torch.equal(fused_seg[lo:hi], separate[s, lo:hi]), s
+
+
+@pytest.mark.parametrize("dtype", HALF)
+def test_moe_equals_unfused_reference_schedule(dtype):
+    """Fused sparse MoE == the reference's schedule run op by op (dense
+    gate and up GEMMs, silu*up, dense down GEMM, route sum)."""
+    gen = torch.Generator(device="cuda").manual_seed(4242)
+    t, e, k, d, i = 333, 6, 2, 256, 320
+    h = _rn(t, d, dtype=dtype, gen=gen)
+    gate = _rn(e, i, d, dtype=dtype, gen=gen, scale=d**-0.5)
+    up = _rn(e, i, d, dtype=dtype, gen=gen, scale=d**-0.5)
+    down = _rn(e, d, i, dtype=dtype, gen=gen, scale=i**-0.5)
+    sel = torch.topk(torch.randn(t, e, device="cuda", generator=gen), k).indices
+    w = torch.rand(t, k, device="cuda", generator=gen).to(dtype)
+    act = moe_mod._silu_mul(moe_mod._expert_bmm(h, gate, 0), moe_mod._expert_bmm(h, up, 0))
+    y = moe_mod._expert_bmm(act, down, act.stride(0))
+    out = torch.empty(t, d, device="cuda", dtype=dtype)
+    lib = _lib.load()
+    _lib.check(lib.bio_moe_route_sum(_lib.DTYPE_CODE[dtype], ctypes.c_void_p(y.data_ptr()),
+                                     _lib.DTYPE_CODE[dtype], ctypes.c_void_p(w.data_ptr()),
+                                     ctypes.c_void_p(sel.contiguous().data_ptr()),
+                                     ctypes.c_void_p(out.data_ptr()), e, t, k, d, 0,
+                                     _lib.stream_of(h)), "bio_moe_route_sum")
+    assert torch.equal(deterministic_token_choice_moe(h, w, sel, gate, up, down), out)
