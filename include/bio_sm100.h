@@ -246,6 +246,21 @@ BIO_API int bio_depthwise_conv1d(int32_t dtype, const void* x, const void* w, co
  * [B][G*Og][in0*k0][in1*k1][in2*k2]; dst = src (+ bias[channel]).  Replaces
  * the bias add and pixel-shuffle permute of conv_transpose2d/3d_batch_invariant
  * (batch_invariant_ops.py:846-861, 926-941). */
+/* Non-overlapping transposed convolution (stride == kernel, no padding,
+ * dilation 1; f16/bf16) in one GEMM whose epilogue writes the final layout:
+ * per (sample, group) C[m = input position, n = (o, kernel offset)] =
+ * sum_c x[b, g*Cg + c, m] * w[g*Cg + c, n] with fixed K order, rounded, plus
+ * bias[g*Og + o] (added after rounding, as the reference's output + bias),
+ * stored at y[b, g*Og + o, s*k + t] (runs of k2 outputs as one vector).  x
+ * [B][C][in...], w [C][Og][k...], y [B][G*Og][in*k...], all contiguous;
+ * prod(in) and Og*prod(k) multiples of 8 (BIO_ERR_ALIGN otherwise; the
+ * caller then uses bio_gemm + bio_conv_transpose_scatter).  Same bits as
+ * that two-step path.  Replaces conv_transpose2d/3d_batch_invariant's bmm,
+ * bias add and permute (batch_invariant_ops.py:783-941). */
+BIO_API int bio_conv_transpose(int32_t dtype, const void* x, const void* w, const void* bias,
+                               void* y, const bio_conv_geom* geom, int64_t out_channels_per_group,
+                               int32_t device, void* stream);
+
 BIO_API int bio_conv_transpose_scatter(int32_t dtype, const void* src, const void* bias,
                                        void* dst, const bio_conv_geom* geom,
                                        int64_t out_channels_per_group, int32_t device,

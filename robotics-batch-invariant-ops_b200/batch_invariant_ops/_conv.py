@@ -7,9 +7,13 @@ out[b, g*Og:(g+1)*Og, L] = W_g[Og, K] @ patches[b, g]^T, bias added per output
 channel in the GEMM epilogue.  The output lands directly in NC[D][H]W layout.
 Depthwise 1-D convolution uses a direct kernel.
 
-Transposed convolution with stride == kernel (padding 0, dilation 1):
-Y[b, g] = W_g^T[Og*kvol, Cg] @ X[b, g][Cg, P] per (sample, group), then
-``bio_conv_transpose_scatter`` does the pixel-shuffle layout and the bias.
+Transposed convolution with stride == kernel (padding 0, dilation 1), the
+reference's orientation (batch_invariant_ops.py:835-861): per (sample,
+group) C[P, Og*kvol] = X[b, g]^T @ W_g, and for 16-bit types one
+``bio_conv_transpose`` GEMM whose epilogue rounds, adds the bias and writes
+each kernel row straight into the output layout.  fp32 (and shapes whose
+sizes break the tensor-map alignment) run the GEMM into a buffer and then
+``bio_conv_transpose_scatter``.
 
 Assertion messages follow the reference (batch_invariant_ops.py:497-941).
 """
@@ -218,6 +222,24 @@ def conv_transpose_nd(input, weight, bias, stride, padding, dilation, output_pad
     p = math.prod(spatial)
     x = input.contiguous()
     w = weight.contiguous()
+    geom = _geom(batch, cin, groups, spatial, ksize, ksize, (0,) * nd, (1,) * nd, spatial)
+    bias_c = bias.contiguous() if bias is not None else None
+    if input.dtype != torch.float32 and cg > 0 and p % 8 == 0 and q % 8 == 0:
+        # one GEMM whose epilogue adds the bias and writes the final layout
+        st = _lib.load().bio_conv_transpose(
+            _lib.DTYPE_CODE[input.dtype],
+            ctypes.c_void_p(x.data_ptr()),
+            ctypes.c_void_p(w.data_ptr()),
+            ctypes.c_void_p(bias_c.data_ptr() if bias_c is not None else 0),
+            ctypes.c_void_p(out.data_ptr()),
+            ctypes.byref(geom),
+            og,
+            input.device.index,
+            _lib.stream_of(input),
+        )
+        if st != _lib.BIO_ERR_ALIGN:
+            _lib.check(st, "bio_conv_transpose")
+            return out
     tmp = torch.empty((batch, groups, q, p), device=input.device, dtype=input.dtype)
     # A[m=q, k=c] = W[g*Cg + c, q]  (M-contiguous);  B[k=c, n=i] = X[b, g*Cg + c, i]
     opa = _gemm.operand_a(w, batch, groups, q, cg, 1, q, 0, cg * q)
@@ -239,8 +261,6 @@ def conv_transpose_nd(input, weight, bias, stride, padding, dilation, output_pad
         )
     else:
         tmp.zero_()
-    geom = _geom(batch, cin, groups, spatial, ksize, ksize, (0,) * nd, (1,) * nd, spatial)
-    bias_c = bias.contiguous() if bias is not None else None
     _lib.check(
         _lib.load().bio_conv_transpose_scatter(
             _lib.DTYPE_CODE[input.dtype],

@@ -101,6 +101,7 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_I32, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _P],
     ),
+    "bio_conv_transpose": (ctypes.c_int, [_I32, _P, _P, _P, _P, _P, _I64, _I32, _P]),
     "bio_conv_transpose_scatter": (ctypes.c_int, [_I32, _P, _P, _P, _P, _I64, _I32, _P]),
     "bio_attention": (ctypes.c_int, [_P, _P]),
     "bio_attention_varlen": (ctypes.c_int, [_P, _P]),

@@ -50,6 +50,14 @@ struct TcGemmParams {
   // accumulator columns [0, 128) hold gate and [128, 256) up for 128 output
   // columns; the epilogue stores round(silu(round(gate)) * round(up)).
   int swiglu;
+  // Transposed-convolution scatter (stride == kernel): tile row m is input
+  // position (s0, s1, s2), column n is (o, t0, t1, t2); the element is
+  // rounded, gets + bias[o] (bias added after rounding, as the reference's
+  // output + bias), and is stored at c + b1*c_s1 + b2*c_s2 + row_off(m) +
+  // col_off(n).  sc_vec: runs of k2 outputs are stored as one vector.
+  int scatter;
+  int sc_s1, sc_s2, sc_k0, sc_k1, sc_k2, sc_kvol, sc_o2, sc_vec;
+  int64_t sc_so, sc_o1o2;
   int64_t batch2;
   int64_t total_tiles;
   int a_div2, b_div2;
@@ -198,6 +206,136 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// ---- transposed-convolution scatter epilogue
+__device__ __forceinline__ int64_t scatter_row_off(const TcGemmParams& p, int m) {
+  const int s2 = m % p.sc_s2;
+  const int r = m / p.sc_s2;
+  const int s1 = r % p.sc_s1;
+  const int s0 = r / p.sc_s1;
+  return static_cast<int64_t>(s0) * p.sc_k0 * p.sc_o1o2 +
+         static_cast<int64_t>(s1) * p.sc_k1 * p.sc_o2 + static_cast<int64_t>(s2) * p.sc_k2;
+}
+
+__device__ __forceinline__ int64_t scatter_col_off(const TcGemmParams& p, int n, int* o) {
+  const int oc = n / p.sc_kvol;
+  const int rem = n - oc * p.sc_kvol;
+  const int k12 = p.sc_k1 * p.sc_k2;
+  const int t0 = rem / k12;
+  const int rem2 = rem - t0 * k12;
+  const int t1 = rem2 / p.sc_k2;
+  const int t2 = rem2 - t1 * p.sc_k2;
+  *o = oc;
+  return static_cast<int64_t>(oc) * p.sc_so + static_cast<int64_t>(t0) * p.sc_o1o2 +
+         static_cast<int64_t>(t1) * p.sc_o2 + t2;
+}
+
+template <typename T>
+__device__ __forceinline__ float scatter_value(float v, const T* bias, int o) {
+  const float x = round_to<T>(v);
+  return bias != nullptr ? x + to_f32(bias[o]) : x;
+}
+
+// K2 contiguous outputs (one kernel row) from v[0 .. K2): pairs rounded with
+// one packed conversion; with a bias, the rounded pair is widened, the bias
+// added in fp32 and the sum rounded again (the reference's output + bias).
+template <typename T>
+__device__ __forceinline__ uint32_t scatter_pair(float lo, float hi, bool has_bias, float bv) {
+  uint32_t w = pack2<T>(lo, hi);
+  if (has_bias) {
+    const T* e = reinterpret_cast<const T*>(&w);
+    w = pack2<T>(to_f32(e[0]) + bv, to_f32(e[1]) + bv);
+  }
+  return w;
+}
+
+template <typename T, int K2>
+__device__ __forceinline__ void store_run(T* dst, const float* v, const T* bias, int o, bool vec) {
+  const bool hb = bias != nullptr;
+  const float bv = hb ? to_f32(bias[o]) : 0.f;
+  if constexpr (K2 == 1) {
+    dst[0] = from_f32<T>(scatter_value<T>(v[0], bias, o));
+  } else {
+    uint32_t w[K2 / 2];
+#pragma unroll
+    for (int i = 0; i < K2 / 2; ++i) w[i] = scatter_pair<T>(v[2 * i], v[2 * i + 1], hb, bv);
+    constexpr int kBytes = K2 * static_cast<int>(sizeof(T));
+    if (vec) {
+      if constexpr (kBytes == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = w[0];
+      } else if constexpr (kBytes == 8) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kBytes / 16; ++q)
+          reinterpret_cast<uint4*>(dst)[q] =
+              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < K2 / 2; ++i) {
+        const T* e = reinterpret_cast<const T*>(&w[i]);
+        dst[2 * i] = e[0];
+        dst[2 * i + 1] = e[1];
+      }
+    }
+  }
+}
+
+// Runs of K2 (a divisor of 32) outputs: the chunk start n0 (a multiple of
+// 32) begins a kernel row (t2 = 0); later runs step (t1, t0, o) without
+// divisions.
+template <typename T, int K2>
+__device__ __forceinline__ void scatter_runs(const TcGemmParams& p, T* cb, int n0,
+                                             const float (&v)[32], const T* bias) {
+  int o;
+  scatter_col_off(p, n0, &o);
+  const int k12 = p.sc_k1 * p.sc_k2;
+  const int rem = n0 - o * p.sc_kvol;
+  int t0 = rem / k12;
+  int t1 = (rem - t0 * k12) / K2;
+#pragma unroll
+  for (int r = 0; r < 32; r += K2) {
+    if (n0 + r < p.n) {  // n is a multiple of k2: runs are whole
+      const int64_t off = static_cast<int64_t>(o) * p.sc_so +
+                          static_cast<int64_t>(t0) * p.sc_o1o2 +
+                          static_cast<int64_t>(t1) * p.sc_o2;
+      store_run<T, K2>(cb + off, v + r, bias, o, p.sc_vec != 0);
+    }
+    if (++t1 == p.sc_k1) {
+      t1 = 0;
+      if (++t0 == p.sc_k0) {
+        t0 = 0;
+        ++o;
+      }
+    }
+  }
+}
+
+// One 32-column chunk of a scatter tile row (cb already holds the row's
+// offset and the batch bases; bias points at this group's channels).
+template <typename T>
+__device__ __forceinline__ void scatter_chunk(const TcGemmParams& p, T* cb, int n0,
+                                              const float (&v)[32], const T* bias) {
+  switch (p.sc_k2) {
+    case 1: scatter_runs<T, 1>(p, cb, n0, v, bias); break;
+    case 2: scatter_runs<T, 2>(p, cb, n0, v, bias); break;
+    case 4: scatter_runs<T, 4>(p, cb, n0, v, bias); break;
+    case 8: scatter_runs<T, 8>(p, cb, n0, v, bias); break;
+    case 16: scatter_runs<T, 16>(p, cb, n0, v, bias); break;
+    case 32: scatter_runs<T, 32>(p, cb, n0, v, bias); break;
+    default:
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (n0 + j < p.n) {
+          int o;
+          const int64_t off = scatter_col_off(p, n0 + j, &o);
+          cb[off] = from_f32<T>(scatter_value<T>(v[j], bias, o));
+        }
+      }
+      break;
+  }
 }
 
 // Bytes of A a CTA loads for a tile: the full 128-row slab, only the valid
@@ -429,6 +567,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m = ti.mb * kBM + q * 32 + lane;
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
                 static_cast<int64_t>(sg.base + m) * p.c_sm;
+      if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -441,6 +580,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+          if (p.scatter) {
+            scatter_chunk<T>(p, crow, n0, v, bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr);
+            continue;
+          }
           if (bias != nullptr) {
             const T* bb = bias + ti.b2 * p.bias_s2;
             if (p.bias_per_row) {
@@ -703,6 +846,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
                 static_cast<int64_t>(sg.base + m) * p.c_sm;
+      if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
       if (p.swiglu) {
         // gate in accumulator columns [0, BNH), up in [BNH, BN); the
         // roundings of separate gate / up GEMMs followed by bio_silu_mul
@@ -759,6 +903,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+          if (p.scatter) {
+            scatter_chunk<T>(p, crow, n0, v, bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr);
+            continue;
+          }
           if (bias != nullptr) {
             const T* bb = bias + ti.b2 * p.bias_s2;
             if (p.bias_per_row) {
@@ -1138,9 +1286,16 @@ int group_rows(int64_t k, int bm, int tiles_m) {
   return static_cast<int>(g);
 }
 
+// Host description of the transposed-convolution scatter epilogue.
+struct ScatterSpec {
+  int s1, s2, k0, k1, k2, o2;
+  int64_t so, o1o2;
+  bool vec;
+};
+
 template <bool PAIR, int BN, bool A_MN, bool B_MN, typename T>
 int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
-              const void* b_up = nullptr) {
+              const void* b_up = nullptr, const ScatterSpec* sc = nullptr) {
   constexpr int STAGES = stages_for<PAIR, BN>();
   constexpr uint32_t kSmem = smem_bytes<PAIR, BN, STAGES>();
   constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
@@ -1237,6 +1392,20 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
   const int out_bn = b_up != nullptr ? BN / 2 : BN;
   p.tiles_n = static_cast<int>((a->n + out_bn - 1) / out_bn);
   p.swiglu = b_up != nullptr ? 1 : 0;
+  p.scatter = 0;
+  if (sc != nullptr) {
+    p.scatter = 1;
+    p.sc_s1 = sc->s1;
+    p.sc_s2 = sc->s2;
+    p.sc_k0 = sc->k0;
+    p.sc_k1 = sc->k1;
+    p.sc_k2 = sc->k2;
+    p.sc_kvol = sc->k0 * sc->k1 * sc->k2;
+    p.sc_o2 = sc->o2;
+    p.sc_vec = sc->vec ? 1 : 0;
+    p.sc_so = sc->so;
+    p.sc_o1o2 = sc->o1o2;
+  }
   p.k_blocks = static_cast<int>((a->k + kBK - 1) / kBK);
   p.group_m = group_rows(a->k, kTileM, p.tiles_m);
   p.a_tail_rows = tail_rows;
@@ -1350,28 +1519,28 @@ bool tile_supported(const TileChoice& tc) {
 
 template <bool A_MN, bool B_MN, typename T>
 int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, const int* seg,
-                cudaStream_t stream) {
+                cudaStream_t stream, const ScatterSpec* sc) {
   if (tc.pair) {
-    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, seg, stream);
-    return launch_tc<true, 256, A_MN, B_MN, T>(a, seg, stream);
+    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, seg, stream, nullptr, sc);
+    return launch_tc<true, 256, A_MN, B_MN, T>(a, seg, stream, nullptr, sc);
   }
   switch (tc.bn) {
-    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream);
-    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream);
-    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream);
-    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream);
+    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream, nullptr, sc);
+    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream, nullptr, sc);
+    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream, nullptr, sc);
+    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream, nullptr, sc);
   }
 }
 
 template <typename T>
 int dispatch_tc(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream, bool a_mn,
-                bool b_mn, const int* seg = nullptr) {
+                bool b_mn, const int* seg = nullptr, const ScatterSpec* sc = nullptr) {
   if (a_mn) {
-    return b_mn ? dispatch_bn<true, true, T>(a, tc, seg, stream)
-                : dispatch_bn<true, false, T>(a, tc, seg, stream);
+    return b_mn ? dispatch_bn<true, true, T>(a, tc, seg, stream, sc)
+                : dispatch_bn<true, false, T>(a, tc, seg, stream, sc);
   }
-  return b_mn ? dispatch_bn<false, true, T>(a, tc, seg, stream)
-              : dispatch_bn<false, false, T>(a, tc, seg, stream);
+  return b_mn ? dispatch_bn<false, true, T>(a, tc, seg, stream, sc)
+              : dispatch_bn<false, false, T>(a, tc, seg, stream, sc);
 }
 
 int launch_f32(const bio_gemm_args* a, cudaStream_t stream) {
@@ -1581,6 +1750,77 @@ int bio_gemm_tiled(const bio_gemm_args* a, int32_t tile_m, int32_t tile_n, void*
 int bio_gemm_segmented(const bio_gemm_args* a, const int32_t* seg, void* stream_v) {
   if (seg == nullptr) return BIO_ERR_ARG;
   return grouped_impl(a, seg, nullptr, stream_v);
+}
+
+int bio_conv_transpose(int32_t dtype, const void* x, const void* w, const void* bias, void* y,
+                       const bio_conv_geom* g, int64_t og, int32_t device, void* stream_v) {
+  if (g == nullptr || og < 1) return BIO_ERR_SHAPE;
+  if (dtype != BIO_F16 && dtype != BIO_BF16) return BIO_ERR_DTYPE;
+  const int64_t nb = g->batch, cin = g->channels, groups = g->groups;
+  if (nb < 0 || cin < 1 || groups < 1 || cin % groups != 0) return BIO_ERR_SHAPE;
+  int64_t p_in = 1, kvol = 1, so = 1;
+  for (int d = 0; d < 3; ++d) {
+    if (g->in[d] < 1 || g->kernel[d] < 1) return BIO_ERR_SHAPE;
+    if (g->stride[d] != g->kernel[d] || g->padding[d] != 0 || g->dilation[d] != 1)
+      return BIO_ERR_ARG;  // non-overlapping (stride == kernel) only
+    p_in *= g->in[d];
+    kvol *= g->kernel[d];
+    so *= g->in[d] * g->kernel[d];
+  }
+  const int64_t cg = cin / groups;
+  const int64_t n = og * kvol;
+  if (nb == 0) return BIO_OK;
+  if (p_in > 2147483647 || n > 2147483647 || cg > 2147483647) return BIO_ERR_SHAPE;
+  if (x == nullptr || w == nullptr || y == nullptr) return BIO_ERR_ARG;
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  // tensor maps: 16-byte aligned bases and strides (P and og*kvol multiples of 8)
+  if (!aligned16(x) || !aligned16(w) || p_in % 8 != 0 || n % 8 != 0) return BIO_ERR_ALIGN;
+  bio_gemm_args a{};
+  a.dtype = dtype;
+  a.flags = 0;
+  a.batch1 = nb;
+  a.batch2 = groups;
+  a.m = p_in;  // A[m = input position, k = c] = x[b, g*cg + c, m]
+  a.n = n;     // B[k = c, n = (o, kernel offset)] = w[g*cg + c, n]
+  a.k = cg;
+  a.a = x;
+  a.a_sm = 1;
+  a.a_sk = p_in;
+  a.a_s1 = cin * p_in;
+  a.a_s2 = cg * p_in;
+  a.a_div2 = 1;
+  a.b = w;
+  a.b_sk = n;
+  a.b_sn = 1;
+  a.b_s1 = 0;
+  a.b_s2 = cg * n;
+  a.b_div2 = 1;
+  a.c = y;
+  a.c_sm = 0;
+  a.c_sn = 0;
+  a.c_s1 = groups * og * so;
+  a.c_s2 = og * so;
+  a.bias = bias;
+  a.bias_s2 = og;
+  a.alpha = 1.0f;
+  a.device = device;
+  ScatterSpec sc;
+  sc.s1 = static_cast<int>(g->in[1]);
+  sc.s2 = static_cast<int>(g->in[2]);
+  sc.k0 = static_cast<int>(g->kernel[0]);
+  sc.k1 = static_cast<int>(g->kernel[1]);
+  sc.k2 = static_cast<int>(g->kernel[2]);
+  sc.o2 = static_cast<int>(g->in[2] * g->kernel[2]);
+  sc.so = so;
+  sc.o1o2 = g->in[1] * g->kernel[1] * g->in[2] * g->kernel[2];
+  sc.vec = aligned16(y);
+  TileChoice tc = pick_tile(p_in, n, nb * groups, bio_host::sm_count(device));
+  if (!tc.pair && tc.bn < 64) tc.bn = 64;  // N-contiguous B: 64-column atoms
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (dtype == BIO_BF16)
+    return dispatch_tc<__nv_bfloat16>(&a, tc, stream, true, true, nullptr, &sc);
+  return dispatch_tc<__half>(&a, tc, stream, true, true, nullptr, &sc);
 }
 
 int bio_gemm_swiglu(const bio_gemm_args* a, const void* up, const int32_t* seg,

@@ -474,3 +474,58 @@ def test_column_mode_vectorised_reductions(dtype):
     assert torch.equal(softmax(x[:1], 1), softmax(x, 1)[:1])
     assert torch.equal(linalg_vector_norm_batch_invariant(x[:1], dim=1),
                        linalg_vector_norm_batch_invariant(x, dim=1)[:1])
+
+
+def _convt_two_step(x, w, b, k, groups):
+    """The buffered path: GEMM into [B, G, Og*kvol, P], then the layout kernel."""
+    import ctypes
+    import math
+
+    from batch_invariant_ops import _conv, _gemm
+
+    nd = x.ndim - 2
+    batch, cin = x.shape[:2]
+    og = w.shape[1]
+    cg = cin // groups
+    kvol = math.prod(k)
+    q, p = og * kvol, math.prod(x.shape[2:])
+    out = torch.empty((batch, og * groups, *(s * kk for s, kk in zip(x.shape[2:], k))),
+                      device="cuda", dtype=x.dtype)
+    tmp = torch.empty((batch, groups, q, p), device="cuda", dtype=x.dtype)
+    xc, wc = x.contiguous(), w.contiguous()
+    opa = _gemm.operand_a(wc, batch, groups, q, cg, 1, q, 0, cg * q)
+    opb = _gemm.operand_b(xc, batch, groups, cg, p, p, 1, cin * p, cg * p)
+    _gemm.launch(opa, opb, tmp, batch1=batch, batch2=groups, m=q, n=p, k=cg, c_sm=p, c_sn=1,
+                 c_s1=groups * q * p, c_s2=q * p)
+    geom = _conv._geom(batch, cin, groups, tuple(x.shape[2:]), k, k, (0,) * nd, (1,) * nd,
+                       tuple(x.shape[2:]))
+    _lib.check(_lib.load().bio_conv_transpose_scatter(
+        _lib.DTYPE_CODE[x.dtype], ctypes.c_void_p(tmp.data_ptr()),
+        ctypes.c_void_p(b.data_ptr() if b is not None else 0), ctypes.c_void_p(out.data_ptr()),
+        ctypes.byref(geom), og, 0, _lib.stream_of(x)), "bio_conv_transpose_scatter")
+    return out
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+@pytest.mark.parametrize(
+    "shape,cout,k,groups,with_bias",
+    [((8, 256, 24, 24), 256, (4, 4), 1, True), ((3, 64, 16, 16), 32, (2, 2), 2, False),
+     ((2, 32, 8, 16), 48, (3, 3), 1, True), ((2, 64, 4, 8), 16, (16, 16), 1, True),
+     ((2, 16, 4, 4, 8), 24, (2, 2, 2), 1, True), ((1, 96, 7, 9), 63, (4, 4), 3, True),
+     ((5, 40, 16, 32), 8, (1, 8), 1, False)],
+)
+def test_fused_conv_transpose_epilogue(dtype, shape, cout, k, groups, with_bias):
+    """The scatter epilogue (one GEMM writing the final layout) equals the
+    buffered GEMM + layout kernel, the oracle and stock torch; shapes with
+    odd sizes take the buffered path and must agree too."""
+    gen = torch.Generator(device="cuda").manual_seed(sum(shape) + cout)
+    x = _rn(*shape, dtype=dtype, gen=gen)
+    w = (_rn(shape[1], cout // groups, *k, gen=gen) * 0.05).to(dtype)
+    b = _rn(cout, dtype=dtype, gen=gen) if with_bias else None
+    nd = len(k)
+    fn = conv_transpose2d_batch_invariant if nd == 2 else conv_transpose3d_batch_invariant
+    out = fn(x, w, b, k, (0,) * nd, (1,) * nd, (0,) * nd, groups)
+    assert torch.equal(out, _convt_two_step(x, w, b, k, groups))
+    assert torch.equal(fn(x[:1], w, b, k, (0,) * nd, (1,) * nd, (0,) * nd, groups), out[:1])
+    tfn = F.conv_transpose2d if nd == 2 else F.conv_transpose3d
+    torch.testing.assert_close(out, tfn(x, w, b, stride=k, groups=groups), **TOLERANCES[dtype])
