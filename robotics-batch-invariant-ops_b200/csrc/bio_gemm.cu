@@ -57,6 +57,9 @@ struct TcGemmParams {
   // col_off(n).  sc_vec: runs of k2 outputs are stored as one vector.
   int scatter;
   int sc_s1, sc_s2, sc_k0, sc_k1, sc_k2, sc_kvol, sc_o2, sc_vec;
+  // plain mode: each epilogue warp stages its 32 x 32 output chunks in
+  // shared memory (64-byte swizzle) and writes them with tensor stores
+  int c_tma;
   int64_t sc_so, sc_o1o2;
   int64_t batch2;
   int64_t total_tiles;
@@ -103,6 +106,8 @@ __device__ __forceinline__ TileIdx decode_tile(int64_t t, int tiles_m, int tiles
 // and an exclusive prefix of m-tiles per segment in shared memory.
 constexpr int kMaxSegs = 1024;
 constexpr uint32_t kSegBytes = 2 * (kMaxSegs + 1) * 4;
+// Epilogue staging for tensor stores: 4 warps x 2 buffers x (32 rows x 64 B).
+constexpr uint32_t kEpiBytes = 4 * 2 * 2048;
 
 struct TileSeg {
   int base, rows;  // first A/C row of the tile's segment and its row count
@@ -338,6 +343,86 @@ __device__ __forceinline__ void scatter_chunk(const TcGemmParams& p, T* cb, int 
   }
 }
 
+// One 32-column chunk of an accumulator row (TMEM words r) of output row m:
+// alpha, then the transposed-convolution scatter, or bias (per column, or
+// per row with BIAS_PER_ROW) and one rounding, 16-byte stores when the row
+// is aligned.  bias already points at this batch's bias vector.
+template <typename T>
+__device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const uint32_t (&r)[32], T* crow,
+                                          int m, int rows, int n0, const T* bias) {
+  if (m >= rows || n0 >= p.n) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  if (p.scatter) {
+    scatter_chunk<T>(p, crow, n0, v, bias);
+    return;
+  }
+  if (bias != nullptr) {
+    if (p.bias_per_row) {
+      const float bv = to_f32(bias[m]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += bv;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.n) v[j] += to_f32(bias[n0 + j]);
+    }
+  }
+  if (p.c_vec_ok && n0 + 32 <= p.n) {
+    uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+      dst[j] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+  }
+}
+
+// Tensor-store form of epi_chunk (plain mode, 16-bit C, no scatter): lane l
+// writes its 32 outputs (64 bytes) as row l of a 32 x 32 staging box with the
+// 64-byte swizzle (16-byte chunk c of row l at chunk c ^ ((l >> 1) & 3)), the
+// layout the tensor map's SWIZZLE_64B expects; rows and columns outside C are
+// clipped by the tensor store.
+template <typename T>
+__device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uint32_t (&r)[32],
+                                                uint8_t* stage, int m, int n0, const T* bias,
+                                                int lane) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  if (bias != nullptr) {
+    if (p.bias_per_row) {
+      const float bv = m < p.m ? to_f32(bias[m]) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += bv;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.n) v[j] += to_f32(bias[n0 + j]);
+    }
+  }
+  uint8_t* row = stage + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 w;
+    w.x = pack2<T>(v[8 * c + 0], v[8 * c + 1]);
+    w.y = pack2<T>(v[8 * c + 2], v[8 * c + 3]);
+    w.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
+    w.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) = w;
+  }
+}
+
 // Bytes of A a CTA loads for a tile: the full 128-row slab, only the valid
 // rows of a partial slab (tail box), or nothing past the end of M.  Rows of
 // the smem slab that are not loaded hold stale data; they only feed output
@@ -362,7 +447,8 @@ struct TcSmem {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kData = STAGES * kStageBytes;
   static constexpr uint32_t kBarBytes = (2 * kMaxStages1 + 5) * 8 + 16;
-  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes + kSegBytes;
+  static constexpr uint32_t kEpiOff = (kData + kBarBytes + kSegBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kTotal = 1024 + kEpiOff + kEpiBytes;
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
@@ -370,7 +456,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA_tail,
                    const __grid_constant__ CUtensorMap tmA5,
-                   const __grid_constant__ CUtensorMap tmB5, const TcGemmParams p) {
+                   const __grid_constant__ CUtensorMap tmB5,
+                   const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
   using L = TcSmem<BN, STAGES>;
   constexpr uint32_t kTmemCols = 2 * BN;
   constexpr uint32_t kIdesc = idesc_f16(TypeFmt<T>::umma, kBM, BN, A_MN, B_MN);
@@ -395,6 +482,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* seg_off = reinterpret_cast<int*>(smem + L::kData + L::kBarBytes);
   int* seg_tiles = seg_off + kMaxSegs + 1;
+  uint8_t* epi_stage = smem + L::kEpiOff;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -555,6 +643,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // -------------------------------- epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int epi_k = 0;  // chunks staged by this warp (tensor-store buffer parity)
     int acc = 0;
     uint32_t acc_phase = 0;
     const T* bias = static_cast<const T*>(p.bias);
@@ -568,49 +657,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
                 static_cast<int64_t>(sg.base + m) * p.c_sm;
       if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) +
-                               (static_cast<uint32_t>(q * 32) << 16),
-                           r);
-        tmem_ld_wait();
-        const int n0 = ti.nb * BN + c0;
-        if (m < sg.rows && n0 < p.n) {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-          if (p.scatter) {
-            scatter_chunk<T>(p, crow, n0, v, bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr);
-            continue;
-          }
-          if (bias != nullptr) {
-            const T* bb = bias + ti.b2 * p.bias_s2;
-            if (p.bias_per_row) {
-              const float bv = to_f32(bb[m]);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += bv;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < p.n) v[j] += to_f32(bb[n0 + j]);
+{
+        const uint32_t tbase =
+            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+        const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+        const int nbase = ti.nb * BN;
+        const int mrow0 = m - lane;  // first output row of this warp
+        auto emit = [&](const uint32_t(&rr)[32], int n0) {
+          if (p.c_tma) {
+            uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
+            if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
             }
-          }
-          if (p.c_vec_ok && n0 + 32 <= p.n) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + n0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 w;
-              w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
-              w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
-              w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
-              w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
-              dst[j] = w;
+            epi_chunk_stage<T>(p, rr, buf, m, n0, bias_b, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (n0 < p.n && mrow0 < p.m)
+                tma_store_4d(&tmC, buf, n0, mrow0, static_cast<int>(ti.b2),
+                             static_cast<int>(ti.b1));
+              bulk_commit();
             }
+            ++epi_k;
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+            epi_chunk<T>(p, rr, crow, m, sg.rows, n0, bias_b);
+          }
+        };
+        if constexpr (BN == 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase, r);
+          tmem_ld_wait_tied(r);
+          emit(r, nbase);
+        } else {
+          // the next 32 columns load while the current ones are converted
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(tbase, ra);
+          tmem_ld_wait_tied(ra);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 64) {
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 32), rb);
+            emit(ra, nbase + c0);
+            tmem_ld_wait_tied(rb);
+            if (c0 + 64 < BN) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 64), ra);
+            emit(rb, nbase + c0 + 32);
+            tmem_ld_wait_tied(ra);
           }
         }
       }
@@ -620,6 +711,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // tensor stores must finish before the CTA (and its staging) goes away
+    if (p.c_tma && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -657,7 +750,8 @@ struct Tc2Smem {
   static constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
   static constexpr uint32_t kData = STAGES * (kABytes + kBBytes);
   static constexpr uint32_t kBarBytes = (2 * kMaxStages2 + 5) * 8 + 16;
-  static constexpr uint32_t kTotal = 1024 + kData + kBarBytes + kSegBytes;
+  static constexpr uint32_t kEpiOff = (kData + kBarBytes + kSegBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kTotal = 1024 + kEpiOff + kEpiBytes;
 };
 
 // Bounded spin on the global timer (used only on the abort path so that copies
@@ -673,7 +767,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA_tail,
-                    const __grid_constant__ CUtensorMap tmB2, const TcGemmParams p) {
+                    const __grid_constant__ CUtensorMap tmB2,
+                    const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
   using L = Tc2Smem<BN, STAGES>;
   constexpr int BNH = BN / 2;
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -696,6 +791,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* seg_off = reinterpret_cast<int*>(smem + L::kData + L::kBarBytes);
   int* seg_tiles = seg_off + kMaxSegs + 1;
+  uint8_t* epi_stage = smem + L::kEpiOff;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -834,6 +930,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else {
     // -------------------------------- epilogue (warps 2..5, both CTAs)
     const int q = warp & 3;
+    int epi_k = 0;  // chunks staged by this warp (tensor-store buffer parity)
     int acc = 0;
     uint32_t acc_phase = 0;
     const T* bias = static_cast<const T*>(p.bias);
@@ -891,49 +988,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         if (acc == 0) acc_phase ^= 1u;
         continue;
       }
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) +
-                               (static_cast<uint32_t>(q * 32) << 16),
-                           r);
-        tmem_ld_wait();
-        const int n0 = ti.nb * BN + c0;
-        if (m < sg.rows && n0 < p.n) {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-          if (p.scatter) {
-            scatter_chunk<T>(p, crow, n0, v, bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr);
-            continue;
-          }
-          if (bias != nullptr) {
-            const T* bb = bias + ti.b2 * p.bias_s2;
-            if (p.bias_per_row) {
-              const float bv = to_f32(bb[m]);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += bv;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < p.n) v[j] += to_f32(bb[n0 + j]);
+{
+        const uint32_t tbase =
+            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+        const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+        const int nbase = ti.nb * BN;
+        const int mrow0 = m - lane;  // first output row of this warp
+        auto emit = [&](const uint32_t(&rr)[32], int n0) {
+          if (p.c_tma) {
+            uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
+            if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
             }
-          }
-          if (p.c_vec_ok && n0 + 32 <= p.n) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + n0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 w;
-              w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
-              w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
-              w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
-              w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
-              dst[j] = w;
+            epi_chunk_stage<T>(p, rr, buf, m, n0, bias_b, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (n0 < p.n && mrow0 < p.m)
+                tma_store_4d(&tmC, buf, n0, mrow0, static_cast<int>(ti.b2),
+                             static_cast<int>(ti.b1));
+              bulk_commit();
             }
+            ++epi_k;
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+            epi_chunk<T>(p, rr, crow, m, sg.rows, n0, bias_b);
+          }
+        };
+        if constexpr (BN == 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase, r);
+          tmem_ld_wait_tied(r);
+          emit(r, nbase);
+        } else {
+          // the next 32 columns load while the current ones are converted
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(tbase, ra);
+          tmem_ld_wait_tied(ra);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 64) {
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 32), rb);
+            emit(ra, nbase + c0);
+            tmem_ld_wait_tied(rb);
+            if (c0 + 64 < BN) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 64), ra);
+            emit(rb, nbase + c0 + 32);
+            tmem_ld_wait_tied(ra);
           }
         }
       }
@@ -943,6 +1042,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // tensor stores must finish before the CTA (and its staging) goes away
+    if (p.c_tma && lane == 0) bulk_wait_all();
   }
 
   // Abort path: give loads already issued (which count on the leader's
@@ -1205,6 +1306,33 @@ int encode_map(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md, 
   CUresult r = enc(map, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
+}
+
+// Output map {n, m, batch2, batch1} of a row-contiguous 16-bit C, box
+// {32, 32, 1, 1}, 64-byte swizzle (the epilogue's staging layout).
+int encode_cmap(CUtensorMap* map, const bio_gemm_args* a) {
+  bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
+  if (enc == nullptr) return BIO_ERR_DRIVER;
+  const CUtensorMapDataType dt =
+      a->dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t row = static_cast<uint64_t>(a->c_sm) * 2;
+  // a batch dimension of extent 1 gets a nominal (valid) stride
+  const uint64_t s2 = a->batch2 > 1 ? static_cast<uint64_t>(a->c_s2) * 2
+                                    : row * static_cast<uint64_t>(a->m);
+  const uint64_t s1 = a->batch1 > 1 ? static_cast<uint64_t>(a->c_s1) * 2
+                                    : s2 * static_cast<uint64_t>(a->batch2);
+  if (row % 16 != 0 || s2 % 16 != 0 || s1 % 16 != 0 || row == 0 || s2 == 0 || s1 == 0)
+    return BIO_ERR_ALIGN;
+  if (row >= (1ull << 40) || s2 >= (1ull << 40) || s1 >= (1ull << 40)) return BIO_ERR_ALIGN;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a->n), static_cast<cuuint64_t>(a->m),
+                        static_cast<cuuint64_t>(a->batch2), static_cast<cuuint64_t>(a->batch1)};
+  cuuint64_t strides[3] = {row, s2, s1};
+  cuuint32_t box[4] = {32, 32, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, a->c, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
 }
 
@@ -1497,6 +1625,15 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
                    ? 1
                    : 0;
   p.status = bio_host::status_word(a->device);
+  // Plain mode writes C through tensor stores when C has a tensor map
+  // (row-contiguous, 16-byte aligned rows and batches, at least one 32 x 32
+  // box); otherwise (and in the segmented, SwiGLU and scatter modes, whose
+  // rows or layout a box cannot express) the epilogue stores directly.
+  CUtensorMap tmC = tmA;
+  p.c_tma = 0;
+  if (seg == nullptr && b_up == nullptr && sc == nullptr && p.c_vec_ok && a->m >= 32 &&
+      a->n >= 32 && encode_cmap(&tmC, a) == BIO_OK)
+    p.c_tma = 1;
 
   const int64_t units = max_units[a->device];
   if (units <= 0) return BIO_ERR_LAUNCH;
@@ -1504,10 +1641,10 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
   const int64_t grid = PAIR ? 2 * n_units : n_units;
   if constexpr (PAIR)
     kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
-                                                                          tmB2, p);
+                                                                          tmB2, tmC, p);
   else
     kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
-                                                                          tmA5, tmB5, p);
+                                                                          tmA5, tmB5, tmC, p);
   return bio_host::launch_status(cudaGetLastError());
 }
 
