@@ -43,7 +43,9 @@ def classify(op: str, shape: dict) -> str | None:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_extended_shapes.py <reference checkout>")
+    ref = Path(sys.argv[1])
     # one case per (model, operator): the largest benchmarked batch
     best: dict[str, dict] = {}
     for path in sorted(glob.glob(str(ref / "research" / "*" / "benchmarks.json"))):

@@ -1,7 +1,7 @@
 """Generate golden vectors by running the REFERENCE implementation on the CPU.
 
 Run in a container where yiannisha/robotics-batch-invariant-ops is checked
-out (path given by --reference, default /root/reference).  Triton kernels run
+out (path given by --reference).  Triton kernels run
 under ``TRITON_INTERPRET=1`` on CPU tensors (fp32 / fp16 GEMMs, softmax,
 log-softmax, attention, conv lowering, mean, vector norm); the MoE runs the
 reference's own CPU branch (moe.py:80-83).  bf16 ``tl.dot`` is not exact
@@ -37,7 +37,7 @@ def _save(name, op, inputs, output, **kwargs):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="reference checkout")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     import triton  # noqa: F401

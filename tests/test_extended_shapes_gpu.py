@@ -1,4 +1,4 @@
-"""Extended shape regression suite (SURVEY row f2): every operator shape the
+"""Extended shape regression suite: every operator shape the
 reference benchmarked on real VLA models (tests/golden/extended_shapes.json,
 extracted from its research/*/benchmarks.json by make_extended_shapes.py) --
 LM heads up to 184,622 wide, Cosmos varlen attention over ~3.1k-token

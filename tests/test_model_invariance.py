@@ -1,4 +1,4 @@
-"""Model-level invariance harness (SURVEY row f1): CPU tests of the report
+"""Model-level invariance harness: CPU tests of the report
 logic with a synthetic adapter (mirroring test_investigation_harness.py:9-70
 of the reference suite), and a GPU test of the random-init pi0-style VLA
 step under set_batch_invariant_mode."""
