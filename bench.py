@@ -35,6 +35,7 @@ bitwise cross-check of the ranks' outputs.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import csv
 import io
 import json
@@ -725,6 +726,122 @@ def run_ops(args) -> None:
           flush=True)
 
 
+def run_vla(args) -> None:
+    """Config 5: the random-init pi0-style VLA step (vision tower, prefix LM,
+    10 flow steps of the action expert) under set_batch_invariant_mode, the
+    batch sharded across ranks (args.vla_batch samples per rank, weak
+    scaling).  Reports samples/s over all ranks (max-over-ranks device time),
+    the same step with the mode off (stock PyTorch: cuBLAS, flash attention)
+    and a bitwise check that sample 0 alone equals sample 0 in the batch."""
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(PKG_ROOT))
+    from batch_invariant_ops import set_batch_invariant_mode
+    from batch_invariant_ops.vla import PiZeroStyleVLA, VLAConfig
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    cfg = VLAConfig.full()
+    model = PiZeroStyleVLA(cfg, dev, seed=0).eval()
+    b = args.vla_batch
+    imgs, ids, noise = [], [], []
+    for i in range(b):  # per global sample index: shards hold different samples
+        g = torch.Generator(device=dev).manual_seed(1000 + rank * b + i)
+        imgs.append(torch.rand(3, cfg.image_size, cfg.image_size, generator=g, device=dev))
+        ids.append(torch.randint(0, cfg.vocab, (cfg.text_tokens,), generator=g, device=dev))
+        noise.append(torch.randn(cfg.chunk, cfg.action_dim, generator=g, device=dev))
+    imgs, ids, noise = torch.stack(imgs), torch.stack(ids), torch.stack(noise)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(mode: bool) -> float:
+        ctx = set_batch_invariant_mode() if mode else contextlib.nullcontext()
+        with torch.inference_mode(), ctx:
+            for _ in range(args.warmup):
+                model(imgs, ids, noise)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                model(imgs, ids, noise)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms_mode = timed(True)
+    clocks = sampler.stop()
+    ms_stock = timed(False)
+    with torch.inference_mode(), set_batch_invariant_mode():
+        full = model(imgs, ids, noise)
+        alone = model(imgs[:1], ids[:1], noise[:1])
+    exact = all(torch.equal(alone[k], full[k][:1]) for k in ("actions", "prefix"))
+    if world > 1:
+        ok = torch.tensor([1 if exact else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        exact = bool(ok.item())
+    if rank == 0:
+        per_sample_flops = _vla_flops(cfg)
+        value = world * b / (ms_mode * 1e-3)
+        print(json.dumps({
+            "metric": "pi0-style VLA step samples/s under set_batch_invariant_mode",
+            "value": round(value, 2), "unit": "samples/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_mode, 3),
+            "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic (random-init weights, U[0,1] images, random ids, N(0,1) noise)",
+            "config": {"workload": "config5-pi0-style-vla", "batch_per_gpu": b,
+                       "global_batch": world * b, "vision": "27 x 1152 (SigLIP-like)",
+                       "prefix_lm": "18 x 2048, GQA 8/1, head 256, GeGLU 16384",
+                       "action_expert": "18 x 1024, 10 flow steps, chunk 50x32",
+                       "parallelism": f"dp{world} (batch sharded, no collective in the step)"},
+            "achieved_tflops": round(per_sample_flops * world * b / (ms_mode * 1e-3) / 1e12, 1),
+            "stock_samples_per_s": round(world * b / (ms_stock * 1e-3), 2),
+            "stock_ms_per_step": round(ms_stock, 3),
+            "first_sample_bitwise_equal_alone_vs_batch": exact,
+            "clocks": clocks,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _vla_flops(cfg) -> float:
+    """Matmul flops of one VLA sample (2 per multiply-add; attention scores
+    and values included, elementwise work excluded)."""
+    p_img = (cfg.image_size // cfg.patch) ** 2
+    t_pre = p_img + cfg.text_tokens
+    hd = cfg.lm_head_dim
+    qkv = (cfg.lm_heads + 2 * cfg.lm_kv_heads) * hd
+    vis = p_img * 3 * cfg.patch * cfg.patch * cfg.vis_width + cfg.vis_layers * (
+        p_img * (4 * cfg.vis_width ** 2 + 2 * cfg.vis_width * cfg.vis_mlp)
+        + 2 * p_img * p_img * cfg.vis_width)
+    vis += p_img * cfg.vis_width * cfg.lm_width
+    lm = cfg.lm_layers * (t_pre * (cfg.lm_width * qkv + cfg.lm_heads * hd * cfg.lm_width
+                                   + 3 * cfg.lm_width * cfg.lm_mlp)
+                          + 2 * t_pre * t_pre * cfg.lm_heads * hd)
+    t_act, t_kv = cfg.chunk, cfg.chunk + t_pre
+    act = cfg.flow_steps * (
+        t_act * (cfg.action_dim + cfg.act_width) * cfg.act_width
+        + cfg.act_layers * (t_act * (cfg.act_width * qkv + cfg.lm_heads * hd * cfg.act_width
+                                     + 3 * cfg.act_width * cfg.act_mlp)
+                            + 2 * t_act * t_kv * cfg.lm_heads * hd)
+        + t_act * cfg.act_width * cfg.action_dim)
+    return 2.0 * (vis + lm + act)
+
+
 def run_profile_point(args) -> None:
     """Minimal launch sequence for ncu captures: one GEMM point (MxN) or one
     attention shape (attn:B,S,causal), 1 + steps launches."""
@@ -783,11 +900,16 @@ def main() -> None:
     parser.add_argument("--triton-ref-worker", action="store_true", help=argparse.SUPPRESS)
     parser.add_argument("--profile-point", default=None, help="MxN: run one GEMM point (for ncu)")
     parser.add_argument("--ops", action="store_true", help="per-operator roofline table")
+    parser.add_argument("--vla", action="store_true",
+                        help="config 5: pi0-style VLA step samples/s under the mode")
+    parser.add_argument("--vla-batch", type=int, default=8, help="VLA samples per GPU")
     parser.add_argument("--ops-filter", default="", help="only --ops cases whose name has this")
     parser.add_argument("--ops-reference", action="store_true",
                         help="with --ops: time the reference package from baseline/_ref")
     args = parser.parse_args()
-    if args.ops:
+    if args.vla:
+        run_vla(args)
+    elif args.ops:
         run_ops(args)
     elif args.profile_point:
         run_profile_point(args)

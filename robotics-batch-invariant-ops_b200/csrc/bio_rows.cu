@@ -413,6 +413,96 @@ __global__ void __launch_bounds__(TEAM >= 128 ? TEAM : 256)
 // slots in increasing c.  CS, gpc and the trees depend on n only.
 constexpr int kClusterTeam = 512;
 
+// RAW (16-bit input, n % 8 == 0, 16-byte aligned rows): the groups stay in
+// registers as their raw 16-byte words (half the registers of floats, two
+// CTAs per SM) and are widened at each use; softmax recomputes the same
+// exponential for the output instead of keeping it.  Every value computed is
+// the one the float form computes, so the two forms give the same bits.
+template <typename TI, typename TO, bool LOG, int CS, int RMAX>
+__global__ void __launch_bounds__(kClusterTeam, 2)
+    row_softmax_cluster_raw_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t n) {
+  constexpr int TEAM = kClusterTeam;
+  __shared__ float scratch[TEAM / 32 + 1];
+  __shared__ float part_max[CS];
+  __shared__ float part_sum[CS];
+  const int t = threadIdx.x;
+  const uint32_t rank = cluster_ctarank();
+  const int64_t r = blockIdx.x / CS;
+  // rows are at most kMaxClusterRow long: group indices fit in int
+  const int groups = static_cast<int>(n / 8);
+  const int gpc = (groups + CS - 1) / CS;
+  const int g_lo = static_cast<int>(rank) * gpc;
+  const int cnt = min(gpc, groups - g_lo);  // groups of this CTA
+  const uint4* row = reinterpret_cast<const uint4*>(x + r * n) + g_lo;
+  uint4 w[RMAX];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q)
+    if (t + q * TEAM < cnt) w[q] = row[t + q * TEAM];
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q) {
+    if (t + q * TEAM < cnt) {
+      const TI* e = reinterpret_cast<const TI*>(&w[q]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, to_f32(e[j]));
+    }
+  }
+  mx = team_reduce<TEAM, true>(mx, scratch);
+  if (t < CS) {
+    const uint32_t dst = mapa_shared(static_cast<uint32_t>(__cvta_generic_to_shared(&part_max[rank])),
+                                     static_cast<uint32_t>(t));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(mx) : "memory");
+  }
+  cluster_sync_all();
+  mx = part_max[0];
+#pragma unroll
+  for (int c = 1; c < CS; ++c) mx = fmaxf(mx, part_max[c]);
+  float den = 0.f;
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q) {
+    if (t + q * TEAM < cnt) {
+      const TI* e = reinterpret_cast<const TI*>(&w[q]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (LOG)
+          den += __expf(to_f32(e[j]) - mx);
+        else
+          den += (mx == -INFINITY) ? 0.f : __expf(to_f32(e[j]) - mx);
+      }
+    }
+  }
+  den = team_reduce<TEAM, false>(den, scratch);
+  if (t < CS) {
+    const uint32_t dst = mapa_shared(static_cast<uint32_t>(__cvta_generic_to_shared(&part_sum[rank])),
+                                     static_cast<uint32_t>(t));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(den) : "memory");
+  }
+  cluster_sync_all();
+  den = part_sum[0];
+#pragma unroll
+  for (int c = 1; c < CS; ++c) den += part_sum[c];
+  TO* out = y + r * n + static_cast<int64_t>(g_lo) * 8;
+  const float lse = LOG ? logf(den) : 0.f;
+  const float inv = den != 0.f ? 1.f / den : 0.f;
+#pragma unroll
+  for (int q = 0; q < RMAX; ++q) {
+    const int gl = t + q * TEAM;
+    if (gl < cnt) {
+      const TI* e = reinterpret_cast<const TI*>(&w[q]);
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = to_f32(e[j]);
+        if (LOG)
+          o[j] = v - mx - lse;
+        else
+          o[j] = ((mx == -INFINITY) ? 0.f : __expf(v - mx)) * inv;
+      }
+      store_group(out, gl, n - static_cast<int64_t>(g_lo) * 8, o);
+    }
+  }
+}
+
 template <typename TI, typename TO, bool LOG, int CS, int RMAX>
 __global__ void __launch_bounds__(kClusterTeam)
     row_softmax_cluster_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t n) {
@@ -650,6 +740,11 @@ int launch_cluster_case(const TI* x, TO* y, int64_t rows, int64_t n, cudaStream_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if constexpr (sizeof(TI) == 2) {
+    if (n % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0)
+      return bio_host::launch_status(cudaLaunchKernelEx(
+          &cfg, bio::row_softmax_cluster_raw_kernel<TI, TO, LOG, CS, RMAX>, x, y, n));
+  }
   return bio_host::launch_status(
       cudaLaunchKernelEx(&cfg, bio::row_softmax_cluster_kernel<TI, TO, LOG, CS, RMAX>, x, y, n));
 }

@@ -529,3 +529,24 @@ def test_fused_conv_transpose_epilogue(dtype, shape, cout, k, groups, with_bias)
     assert torch.equal(fn(x[:1], w, b, k, (0,) * nd, (1,) * nd, (0,) * nd, groups), out[:1])
     tfn = F.conv_transpose2d if nd == 2 else F.conv_transpose3d
     torch.testing.assert_close(out, tfn(x, w, b, stride=k, groups=groups), **TOLERANCES[dtype])
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+@pytest.mark.parametrize("n", (16392, 40000, 65536, 131072, 257152, 262144))
+@pytest.mark.parametrize("log", (False, True))
+def test_cluster_softmax_register_forms_agree(dtype, n, log):
+    """Long rows: aligned 16-bit rows keep raw words in registers, unaligned
+    rows keep floats; both forms must give the same bits."""
+    gen = torch.Generator(device="cuda").manual_seed(n + int(log))
+    rows = 3
+    buf = (torch.randn(rows * n + 8, device="cuda", generator=gen) * 4).to(dtype)
+    aligned = buf[: rows * n].view(rows, n)
+    unaligned = buf[1 : 1 + rows * n].view(rows, n)  # 2-byte offset
+    ref_input = unaligned.clone()                   # aligned copy of the same values
+    fn = log_softmax if log else softmax
+    a = fn(ref_input, -1)
+    b = fn(unaligned, -1)
+    assert torch.equal(a, b)
+    assert torch.equal(fn(aligned[1:2].clone(), -1), fn(aligned, -1)[1:2])
+    ref = O.log_softmax(ref_input, -1) if log else O.softmax(ref_input, -1)
+    _close_to_oracle(a, ref, dtype)
