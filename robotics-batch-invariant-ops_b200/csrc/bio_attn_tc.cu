@@ -604,12 +604,28 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
                                 p.status);
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
+        // whole 32-column chunks of an aligned row leave as four 16-byte
+        // stores (the same roundings as the element stores)
+        const bool vec_row = row_valid && (reinterpret_cast<uintptr_t>(out_row) & 15u) == 0;
 #pragma unroll 1
         for (int c = half * (DVP / 32 / HALVES); c < (half + 1) * (DVP / 32 / HALVES); ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem + lane_base + kOCol + static_cast<uint32_t>(c * 32), v);
           tmem_ld_wait();
-          if (row_valid) {
+          if (vec_row && c * 32 + 32 <= p.dv) {
+            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = q4 * 8 + 2 * e;
+                w[e] = pack_pair<T>(l > 0.f ? __uint_as_float(v[j]) / l : 0.f,
+                                    l > 0.f ? __uint_as_float(v[j + 1]) / l : 0.f);
+              }
+              dst[q4] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else if (row_valid) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int col = c * 32 + j;
