@@ -1134,13 +1134,41 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
       // masked, -inf past the visible range), one 32-column chunk at a time,
       // so the mask code never holds the whole row in registers.
       if (!plain) {
+        const uint8_t* mrow_p = static_cast<const uint8_t*>(p.mask) + mrow + col0;
+        if (p.mask_kind == 1 && p.m_sk == 1 && col0 + kAtBN <= lk_seq &&
+            (reinterpret_cast<uintptr_t>(mrow_p) & 15u) == 0) {
+          // boolean mask, whole block in bounds: the row's 128 mask bytes are
+          // loaded up front (one memory latency per block), then applied
+          // chunk by chunk exactly as apply_mask_chunk does
+          uint4 mw[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mw[q] = reinterpret_cast<const uint4*>(mrow_p)[q];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t g[32];
+            tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+            tmem_ld_wait();
+            const uint32_t wd[8] = {mw[2 * c].x,     mw[2 * c].y,     mw[2 * c].z,
+                                    mw[2 * c].w,     mw[2 * c + 1].x, mw[2 * c + 1].y,
+                                    mw[2 * c + 1].z, mw[2 * c + 1].w};
+            const int lim = nvis - c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const bool keep = ((wd[j >> 2] >> ((j & 3) * 8)) & 0xffu) != 0;
+              const float sv = (j < lim && keep) ? __uint_as_float(g[j]) * p.scale : -INFINITY;
+              g[j] = __float_as_uint(sv);
+            }
+            tmem_st_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+          }
+        } else {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t g[32];
-          tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
-          tmem_ld_wait();
-          apply_mask_chunk(p, g, mrow, col0 + c * 32, nvis - c * 32, lk_seq);
-          tmem_st_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+          for (int c = 0; c < 4; ++c) {
+            uint32_t g[32];
+            tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+            tmem_ld_wait();
+            apply_mask_chunk(p, g, mrow, col0 + c * 32, nvis - c * 32, lk_seq);
+            tmem_st_32x32b_x32(s_addr + static_cast<uint32_t>(c * 32), g);
+          }
         }
         tmem_st_wait();
       }
