@@ -1366,7 +1366,8 @@ int encode_map5(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md,
 //              widest of 128/64/32 that still spreads over half the SMs
 //   otherwise  CTA pair, 256 x 256 (1/128 byte of operands per flop and SM),
 //              or single-CTA 128 x 128 when the pair grid would cover less
-//              than a quarter of the SMs
+//              than a quarter of the SMs, or single-CTA 128 x 256 when that
+//              tiling needs fewer waves over the SMs
 struct TileChoice {
   bool pair;
   int bn;
@@ -1381,6 +1382,16 @@ TileChoice pick_tile(int64_t m, int64_t n, int64_t batch, int sms) {
   if (n <= 64) return {false, 64};
   const int64_t pair_tiles = batch * ((m + 255) / 256) * ((n + 255) / 256);
   if (pair_tiles * 4 < sms) return {false, 128};
+  // Wave count: a wave of single-CTA 128 x 256 tiles does the work of a wave
+  // of pair tiles at ~1.11x the time (measured), so the single-CTA tiling
+  // wins only when it needs fewer waves -- M an odd multiple of 128 leaves
+  // the last pair tile of every column half empty (e.g. a 1152-channel
+  // convolution: 3 pair waves against 2 single-CTA waves).
+  const int64_t pairs = sms / 2 > 0 ? sms / 2 : 1;
+  const int64_t one_tiles = batch * ((m + 127) / 128) * ((n + 255) / 256);
+  const int64_t waves_pair = (pair_tiles + pairs - 1) / pairs;
+  const int64_t waves_one = (one_tiles + sms - 1) / sms;
+  if (waves_one * 10 < waves_pair * 9) return {false, 256};
   return {true, 256};
 }
 
