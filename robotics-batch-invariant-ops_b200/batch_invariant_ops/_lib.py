@@ -162,7 +162,15 @@ def check(status: int, what: str) -> None:
         raise RuntimeError(f"{what} failed: {status_message(status)} (status {status})")
 
 
+# Current-stream lookup without building a torch.cuda.Stream object per call
+# (the raw handle of the same current stream); the public API otherwise.
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(tensor: torch.Tensor) -> ctypes.c_void_p:
+    """The current CUDA stream of ``tensor``'s device, as the C ABI takes it."""
+    if _RAW_STREAM is not None:
+        return ctypes.c_void_p(_RAW_STREAM(tensor.device.index))
     return ctypes.c_void_p(torch.cuda.current_stream(tensor.device).cuda_stream)
 
 
