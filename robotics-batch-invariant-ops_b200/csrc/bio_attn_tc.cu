@@ -282,8 +282,12 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
   uint8_t* sV = sK + S * L::kK;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * L::kV);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;      // [S]
-  uint64_t* kv_empty = bars + 3;     // [S]
+  // K and V of a stage have their own barriers: K_{j+1} is copied as soon
+  // as S_j has consumed K_j, while softmax_j and PV_j still run
+  uint64_t* k_full = bars + 1;       // [S]
+  uint64_t* k_empty = bars + 3;      // [S]
+  uint64_t* v_full = bars + 18;      // [S]
+  uint64_t* v_empty = bars + 20;     // [S]
   uint64_t* s_full = bars + 5;       // [2]
   uint64_t* s_free = bars + 7;       // [2]
   uint64_t* p_ready = bars + 9;
@@ -298,8 +302,10 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < S; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
@@ -334,27 +340,34 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
       mbar_arrive_expect_tx(q_full, L::kQ);
       for (int c = 0; c < kQChunks; ++c)
         tma_load_4d(sQ + c * 16384, &tmQ, q_full, c * 64, qc, hc, bc);
-      int issued = 0;
+      int k_issued = 0, v_issued = 0;
       for (int jb = 0; jb < nblk; ++jb) {
         const int stage = jb % S;
         const uint32_t ph = static_cast<uint32_t>(jb / S) & 1u;
-        if (!at_wait(&kv_empty[stage], ph ^ 1u, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(&kv_full[stage], L::kK + L::kV);
-        uint8_t* k_dst = sK + stage * L::kK;
-        uint8_t* v_dst = sV + stage * L::kV;
         const int row = kc0 + jb * kAtBN;
+        if (!at_wait(&k_empty[stage], ph ^ 1u, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&k_full[stage], L::kK);
+        uint8_t* k_dst = sK + stage * L::kK;
         for (int c = 0; c < kQChunks; ++c)
-          tma_load_4d(k_dst + c * 16384, &tmK, &kv_full[stage], c * 64, row, hkc, bc);
+          tma_load_4d(k_dst + c * 16384, &tmK, &k_full[stage], c * 64, row, hkc, bc);
+        k_issued = jb + 1;
+        if (!at_wait(&v_empty[stage], ph ^ 1u, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&v_full[stage], L::kV);
+        uint8_t* v_dst = sV + stage * L::kV;
         for (int kcnk = 0; kcnk < 2; ++kcnk)
           for (int nc = 0; nc < kVChunks; ++nc)
-            tma_load_4d(v_dst + (kcnk * kVChunks + nc) * 8192, &tmV, &kv_full[stage], nc * 64,
+            tma_load_4d(v_dst + (kcnk * kVChunks + nc) * 8192, &tmV, &v_full[stage], nc * 64,
                         row + kcnk * 64, hkc, bc);
-        ++issued;
+        v_issued = jb + 1;
       }
       // drain: Q and the last loads of each stage must land before exit
       if (!at_wait_drain(q_full, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
-      for (int jb = issued - 1; jb >= 0 && jb >= issued - S; --jb) {
-        if (!at_wait_drain(&kv_full[jb % S], static_cast<uint32_t>(jb / S) & 1u))
+      for (int jb = k_issued - 1; jb >= 0 && jb >= k_issued - S; --jb) {
+        if (!at_wait_drain(&k_full[jb % S], static_cast<uint32_t>(jb / S) & 1u))
+          raise_status(p.status, BIO_DEV_TIMEOUT);
+      }
+      for (int jb = v_issued - 1; jb >= 0 && jb >= v_issued - S; --jb) {
+        if (!at_wait_drain(&v_full[jb % S], static_cast<uint32_t>(jb / S) & 1u))
           raise_status(p.status, BIO_DEV_TIMEOUT);
       }
     }
@@ -364,7 +377,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
       bool ok = at_wait(q_full, 0, abort_flag, p.status);
       auto issue_s = [&](int jb) -> bool {
         const int stage = jb % S;
-        if (!at_wait(&kv_full[stage], static_cast<uint32_t>(jb / S) & 1u, abort_flag, p.status))
+        if (!at_wait(&k_full[stage], static_cast<uint32_t>(jb / S) & 1u, abort_flag, p.status))
           return false;
         const int sb = jb & 1;
         if (!at_wait(&s_free[sb], (static_cast<uint32_t>(jb >> 1) & 1u) ^ 1u, abort_flag,
@@ -379,19 +392,19 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
                    smem_desc_sw128(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[stage]);  // K_jb is free once S_jb is done
         return true;
       };
-      const bool ahead = S >= 2;
-      if (ok && ahead) ok = issue_s(0);
+      // S_{j+1} is issued before PV_j (its K copy overlaps softmax_j); the
+      // softmax waits for PV_{j-1} before it rewrites P
+      if (ok) ok = issue_s(0);
       for (int jb = 0; ok && jb < nblk; ++jb) {
-        if (ahead) {
-          if (jb + 1 < nblk && !issue_s(jb + 1)) break;
-        } else if (!issue_s(jb)) {
-          break;
-        }
+        if (jb + 1 < nblk && !issue_s(jb + 1)) break;
         if (!at_wait(p_ready, static_cast<uint32_t>(jb) & 1u, abort_flag, p.status)) break;
-        tc_fence_after();
         const int stage = jb % S;
+        if (!at_wait(&v_full[stage], static_cast<uint32_t>(jb / S) & 1u, abort_flag, p.status))
+          break;
+        tc_fence_after();
         const uint32_t pa = smem_u32(sP), va = smem_u32(sV + stage * L::kV);
 #pragma unroll
         for (int kk = 0; kk < kAtBN / 16; ++kk) {
@@ -400,7 +413,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
           umma_f16(tmem + kOCol, smem_desc_sw128(pa + aoff, 16, 1024),
                    smem_desc_sw128(va + boff, 8192, 1024), kIdescO, (jb | kk) != 0 ? 1u : 0u);
         }
-        umma_commit(&kv_empty[stage]);
+        umma_commit(&v_empty[stage]);
         umma_commit(pv_done);
       }
       umma_commit(mma_done);
