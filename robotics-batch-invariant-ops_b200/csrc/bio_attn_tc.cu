@@ -1318,23 +1318,31 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        const bool vec = row_valid && p.dv == D &&
-                         (reinterpret_cast<uintptr_t>(out_row) & 15u) == 0;
+        // aligned rows leave as 16-byte groups of 8 columns (a head dim that
+        // is not a multiple of 8 ends with element stores); same roundings
+        const bool vec = row_valid && (reinterpret_cast<uintptr_t>(out_row) & 15u) == 0;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(o_addr + static_cast<uint32_t>(c * 32), v);
           tmem_ld_wait();
           if (vec) {
-            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
-              uint32_t w[4];
+              const int col = c * 32 + q4 * 8;
+              if (col + 8 <= p.dv) {
+                uint32_t w[4];
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                w[e] = pack_pair<T>(__uint_as_float(v[q4 * 8 + 2 * e]) * inv,
-                                    __uint_as_float(v[q4 * 8 + 2 * e + 1]) * inv);
-              dst[q4] = make_uint4(w[0], w[1], w[2], w[3]);
+                for (int e = 0; e < 4; ++e)
+                  w[e] = pack_pair<T>(__uint_as_float(v[q4 * 8 + 2 * e]) * inv,
+                                      __uint_as_float(v[q4 * 8 + 2 * e + 1]) * inv);
+                *reinterpret_cast<uint4*>(out_row + col) = make_uint4(w[0], w[1], w[2], w[3]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (col + e < p.dv)
+                    out_row[col + e] = from_f32<T>(__uint_as_float(v[q4 * 8 + e]) * inv);
+              }
             }
           } else if (row_valid) {
 #pragma unroll
