@@ -322,6 +322,22 @@ def test_sdpa_matches_torch_and_oracle(dtype, causal):
     _close_to_oracle(out, O.sdpa(q, k, v, None, causal), dtype)
 
 
+@pytest.mark.parametrize("head_dim", (52, 72, 100))
+def test_sdpa_two_tile_head_dims_below_padded_width(head_dim):
+    # more than 128 query rows and equal padded widths take the two-tile kernel;
+    # 52 and 100 end in a partial group of 8 output columns
+    gen = torch.Generator(device="cuda").manual_seed(7230 + head_dim)
+    q = _rn(3, 2, 300, head_dim, dtype=torch.bfloat16, gen=gen)
+    k = _rn(3, 2, 300, head_dim, dtype=torch.bfloat16, gen=gen)
+    v = _rn(3, 2, 300, head_dim, dtype=torch.bfloat16, gen=gen)
+    out = scaled_dot_product_attention_batch_invariant(q, k, v)
+    torch.testing.assert_close(out, F.scaled_dot_product_attention(q, k, v),
+                               **TOLERANCES[torch.bfloat16])
+    _close_to_oracle(out, O.sdpa(q, k, v, None, False), torch.bfloat16)
+    alone = scaled_dot_product_attention_batch_invariant(q[:1], k[:1], v[:1])
+    assert_first_sample_equal(alone, out)
+
+
 @pytest.mark.parametrize("mask_kind", ("boolean", "additive"))
 def test_sdpa_matches_torch_with_mask(mask_kind):
     gen = torch.Generator(device="cuda").manual_seed(7250)
