@@ -44,7 +44,7 @@ extern "C" {
 #define BIO_ERR_DRIVER 6      /* driver entry point or tensor map failure    */
 #define BIO_ERR_ARG 7         /* invalid argument value (null ptr, flags)    */
 #define BIO_ERR_DEVICE 8      /* a device-side check fired (see status word) */
-#define BIO_ERR_SCRATCH 9     /* problem needs more than the fixed scratch     */
+#define BIO_ERR_SCRATCH 9     /* scratch / workspace too small for the problem */
 
 /* ---- device status word bits (set by kernels, read by the host) -------- */
 #define BIO_DEV_TIMEOUT 1     /* a bounded mbarrier wait gave up             */
@@ -78,14 +78,20 @@ BIO_API int bio_clear_device_status(int device);
  * A element (m, k) at a_sm*m + a_sk*k; B element (k, n) at b_sk*k + b_sn*n;
  * C element (m, n) at c_sm*m + c_sn*n.
  *
- * fp32 runs on CUDA cores with IEEE fp32 FMA in sequential k order (no TF32).
- * bf16/fp16 run on tcgen05 tensor cores with fp32 accumulation; A must be
- * K-contiguous (a_sk == 1) or M-contiguous (a_sm == 1) and B K-contiguous
- * (b_sk == 1) or N-contiguous (b_sn == 1), with 16-byte aligned pointers and
- * strides (BIO_ERR_ALIGN otherwise; the caller packs with bio_pack_rows).
- * The tile shape and K order are chosen from (n, k, dtype) only: the result
- * of row m never depends on m, on M or on the batch count.  Bias is added in
- * fp32 after the full K reduction, then the sum is rounded to the C dtype.
+ * fp32 runs on CUDA cores: exact fp64 products summed with fp64 FMA in
+ * sequential k order, one rounding to fp32 (no TF32); bio_gemm_f32_exact
+ * below is the faster fp32 path.  bf16/fp16 run on tcgen05 tensor cores with
+ * fp32 accumulation; A must be K-contiguous (a_sk == 1) or M-contiguous
+ * (a_sm == 1) and B K-contiguous (b_sk == 1) or N-contiguous (b_sn == 1),
+ * with 16-byte aligned pointers and strides (BIO_ERR_ALIGN otherwise; the
+ * caller packs with bio_pack_rows).  Every output element is accumulated in
+ * the same fixed sequence (64-wide K blocks in increasing order, four K=16
+ * MMAs per block into one fp32 accumulator, one rounding); the output tile,
+ * which bio_gemm_tile_for reports, is picked from m, n, the batch count and
+ * the SM count and only decides which SM computes which elements, so the
+ * result of row m never depends on m, on M or on the batch count.  Bias is
+ * added in fp32 after the full K reduction, then the sum is rounded to the C
+ * dtype.
  *
  * Replaces matmul_kernel_persistent / matmul_persistent
  * (batch_invariant_ops.py:61-139, 271-343) and bmm_kernel_persistent /
@@ -113,10 +119,20 @@ BIO_API int bio_gemm(const bio_gemm_args* args, void* stream);
 
 /* Configuration id for (n, k, dtype): the large-M output tile and the K block
  * whose fixed order defines every output element's accumulation.  Encodes
- * block_m * 1000000 + block_n * 1000 + block_k.  The output tile of a call
- * may also depend on m (small m streams B with narrower tiles); all tiles run
- * the same per-element sequence, which bio_gemm_tiled lets tests check. */
+ * block_m * 1000000 + block_n * 1000 + block_k.  The output tile of a given
+ * call also depends on m (bio_gemm_tile_for); all tiles run the same
+ * per-element sequence, which bio_gemm_tiled lets tests check. */
 BIO_API int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype);
+
+/* The output tile bio_gemm runs (f16/bf16 tensor-core path) for an m x n
+ * GEMM over `batch` independent products on a device with `sms` SMs, with B
+ * N-contiguous when b_mn != 0: *tile_m 128 (one CTA) or 256 (CTA pair),
+ * *tile_n 32..256.  Pure function, needs no GPU.  BIO_ERR_ARG for a null
+ * pointer or a non-positive size.  No counterpart in the reference (its
+ * matmul_persistent, batch_invariant_ops.py:294-319, has one tile per
+ * dtype). */
+BIO_API int bio_gemm_tile_for(int64_t m, int64_t n, int64_t batch, int32_t sms, int32_t b_mn,
+                              int32_t* tile_m, int32_t* tile_n);
 
 /* Workspace bytes that bio_gemm_f32_exact needs for these arguments; 0 when
  * that path does not apply (dtype not BIO_F32, K == 0 or K > 65536, empty or
@@ -381,6 +397,21 @@ BIO_API int bio_moe_route_sum_sorted(int32_t dtype, const void* y_sorted, int32_
                                      int64_t experts, int64_t tokens, int64_t top_k,
                                      int64_t hidden, int32_t device, void* stream);
 
+/* ---- failure detection self-test -----------------------------------------
+ * Runs the bounded-wait exit path of the pipelined kernels on purpose: one
+ * CTA with a TMA producer and a consumer on a two-stage ring (the same
+ * mbar_wait / mbar_wait_drain the GEMM and attention kernels use), in which
+ * the consumer never releases a stage and then waits on a barrier nothing
+ * arrives at.  Both waits give up after `timeout_ns` (1 us .. 2 s); the
+ * kernel raises BIO_DEV_TIMEOUT in the status word, drains its two copies
+ * (src: 8192 bytes, 16-byte aligned, device memory), frees its tensor
+ * memory and returns, so the context stays usable.  `out` (device int32[4])
+ * receives: producer gave up, consumer gave up, stage 0 landed intact, drain
+ * completed (1 each when the path works).  No counterpart in the reference,
+ * whose MoE index check is a trapping device assert (moe.py:67-74). */
+BIO_API int bio_selftest_bounded_wait(const void* src, int32_t* out, int64_t timeout_ns,
+                                      int32_t device, void* stream);
+
 /* ---- convolution that allocates nothing ---------------------------------
  * No counterpart in the reference (its convolutions allocate their im2col
  * buffers through PyTorch on every call).  This entry point is for callers
@@ -390,21 +421,29 @@ BIO_API int bio_moe_route_sum_sorted(int32_t dtype, const void* y_sorted, int32_
  * allocator, and code running inside another runtime's stream capture where
  * allocation calls are not permitted.
  *
- * Same result as bio_im2col + bio_gemm (regular N-d convolution, any groups,
- * stride, padding, dilation; bias per output channel): the patch matrix, and a
- * zero-padded copy of the weight when its rows are not 16-byte aligned, are
- * kept in ONE file-scope device array of BIO_NOALLOC_SCRATCH_BYTES (32 MiB)
- * that every GPU which loads the library holds until the process exits.
+ * Same bits as the regular path (bio_im2col, then bio_gemm for f16/bf16 or
+ * bio_gemm_f32_exact for fp32, K <= 65536; regular N-d convolution, any
+ * groups, stride, padding, dilation; bias per output channel): the patch
+ * matrix, a zero-padded copy of the weight when its rows are not 16-byte
+ * aligned, and (fp32) the exact GEMM's digit workspace are kept in ONE
+ * file-scope device array of BIO_NOALLOC_SCRATCH_BYTES (32 MiB) that every
+ * GPU which loads the library holds until the process exits.
  * The caller passes contiguous x [B][C][in...], weight [O][C/G][kernel...],
- * bias [O] or NULL and y [B][O][out...].  Problems needing more scratch
+ * bias [O] or NULL and y [B][O][out...].  geom->out must be the extent the
+ * geometry implies, (in + 2*pad - dil*(kernel-1) - 1) / stride + 1 per dim
+ * (BIO_ERR_SHAPE otherwise).  Problems needing more scratch
  * (B*G*prod(out)*roundup8(C/G*prod(kernel))*dtype bytes, plus the padded
- * weight) return BIO_ERR_SCRATCH before anything is launched.
+ * weight or the fp32 workspace) return BIO_ERR_SCRATCH before anything is
+ * launched; every size is checked against overflow before it is compared.
  * The first call on a device looks up the array's device address (module
- * load); make that first call before any stream capture.  Every call shares
- * the array, so calls that may overlap on the GPU (different streams, or
- * different host threads on one device) race on it: serialise them.  Nothing
- * in the array needs to start at zero (every byte used is written first).
- * Never calls cudaMalloc, cudaFree or an allocating library routine. */
+ * load) and caches it; make that first call before any stream capture.  The
+ * cached address belongs to the device's primary context: after
+ * cudaDeviceReset the process must not call this entry point again.  Every
+ * call shares the array, so calls that may overlap on the GPU (different
+ * streams, or different host threads on one device) race on it: serialise
+ * them.  Nothing in the array needs to start at zero (every byte used is
+ * written first).  Never calls cudaMalloc, cudaFree or an allocating
+ * library routine. */
 #define BIO_NOALLOC_SCRATCH_BYTES (32ull << 20)
 BIO_API int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* weight,
                                 const void* bias, void* y, const bio_conv_geom* geom,

@@ -166,23 +166,38 @@ def log_softmax(x, dim=-1):
 # ---------------------------------------------------------------------------
 # Attention
 # ---------------------------------------------------------------------------
-def sdpa(q, k, v, attn_mask=None, is_causal=False, scale=None, enable_gqa=False):
+def sdpa(q, k, v, attn_mask=None, is_causal=False, scale=None, enable_gqa=False,
+         query_rows=None):
     """Eager attention of scaled_dot_product_attention_batch_invariant
     (:1148-1213): GQA by repeating KV heads, top-left causal mask, boolean
-    masks drop keys, float masks add; fully masked rows produce 0."""
+    masks drop keys, float masks add; fully masked rows produce 0.
+
+    ``query_rows`` (optional 1-D index tensor) evaluates only those query
+    positions: the result is [..., len(query_rows), Dv], row r holding query
+    position query_rows[r] with its causal/mask row at that absolute position
+    (each query row is independent, so this is exactly the same arithmetic
+    as the full evaluation restricted to those rows)."""
     q64, k64, v64 = _f64(q), _f64(k), _f64(v)
+    lq_full = q64.shape[-2]
+    rows = None
+    if query_rows is not None:
+        rows = torch.as_tensor(query_rows, dtype=torch.long).reshape(-1).cpu()
+        q64 = q64.index_select(-2, rows)
     if enable_gqa:
         rep = q64.shape[-3] // k64.shape[-3]
         k64 = k64.repeat_interleave(rep, dim=-3)
         v64 = v64.repeat_interleave(rep, dim=-3)
-    lq, lk = q64.shape[-2], k64.shape[-2]
+    lk = k64.shape[-2]
     s = scale if scale is not None else 1.0 / math.sqrt(q64.shape[-1])
     scores = (q64 @ k64.transpose(-1, -2)) * s
+    qpos = rows if rows is not None else torch.arange(lq_full)
     if is_causal:
-        keep = torch.ones(lq, lk, dtype=torch.bool).tril()
+        keep = torch.arange(lk)[None, :] <= qpos[:, None]
         scores = scores.masked_fill(~keep, -math.inf)
     elif attn_mask is not None:
         m = attn_mask.detach().cpu()
+        if rows is not None and m.shape[-2] != 1:
+            m = m.index_select(-2, rows)
         if m.dtype == torch.bool:
             scores = scores.masked_fill(~m, -math.inf)
         else:
@@ -190,10 +205,14 @@ def sdpa(q, k, v, attn_mask=None, is_causal=False, scale=None, enable_gqa=False)
     return softmax(scores, dim=-1) @ v64
 
 
-def varlen_sdpa(q, k, v, cu_q, cu_kv, is_causal=False, causal_type=None, scale=None):
+def varlen_sdpa(q, k, v, cu_q, cu_kv, is_causal=False, causal_type=None, scale=None,
+                query_tokens=None):
     """Packed-sequence attention (:1216-1344): each (q segment, kv segment)
     pair attends independently; rows outside every segment and segments with
-    an empty KV range stay zero; TopLeft / BottomRight causal alignment."""
+    an empty KV range stay zero; TopLeft / BottomRight causal alignment.
+
+    ``query_tokens`` (optional iterable of packed query token indices)
+    evaluates only those tokens; the other rows of the result stay zero."""
     q64, k64, v64 = _f64(q), _f64(k), _f64(v)
     cq = [int(t) for t in cu_q.detach().cpu().tolist()]
     ck = [int(t) for t in cu_kv.detach().cpu().tolist()]
@@ -201,24 +220,33 @@ def varlen_sdpa(q, k, v, cu_q, cu_kv, is_causal=False, causal_type=None, scale=N
     name = getattr(causal_type, "name", causal_type)
     if name is not None:
         name = str(name).rsplit(".", 1)[-1]
+    wanted = None
+    if query_tokens is not None:
+        wanted = sorted({int(t) for t in query_tokens})
     for i in range(len(cq) - 1):
         qs, qe, ks, ke = cq[i], cq[i + 1], ck[i], ck[i + 1]
         lq, lk = qe - qs, ke - ks
         if lq == 0 or lk == 0:
             continue
+        local = None
+        if wanted is not None:
+            local = [t - qs for t in wanted if qs <= t < qe]
+            if not local:
+                continue
+        qpos = torch.tensor(local) if local is not None else torch.arange(lq)
         qi = q64[:, qs:qe].transpose(1, 2)
         ki = k64[:, ks:ke].transpose(1, 2)
         vi = v64[:, ks:ke].transpose(1, 2)
         mask = None
         causal = is_causal
         if is_causal and lq != lk:
-            qidx = torch.arange(lq)[:, None]
             kidx = torch.arange(lk)[None, :]
             shift = lk - lq if name == "BottomRight" else 0
-            mask = kidx <= qidx + shift
+            mask = kidx <= torch.arange(lq)[:, None] + shift
             causal = False
-        o = sdpa(qi, ki, vi, mask, causal, scale, enable_gqa=qi.shape[1] != ki.shape[1])
-        out[:, qs:qe] = o.transpose(1, 2)
+        o = sdpa(qi, ki, vi, mask, causal, scale, enable_gqa=qi.shape[1] != ki.shape[1],
+                 query_rows=qpos)
+        out[:, qs + qpos] = o.transpose(1, 2)
     return out
 
 
@@ -243,19 +271,29 @@ def vector_norm(x, dims: Sequence[int] | None, keepdim=False):
 # ---------------------------------------------------------------------------
 def moe(hidden, routing_weights, selected_experts, gate_w, up_w, down_w):
     """Top-k SwiGLU MoE (moe.py:11-92): for each token, sum over its k routes
-    (left to right) of w * down(silu(gate h) * (up h)) of the selected expert."""
+    (left to right) of w * down(silu(gate h) * (up h)) of the selected expert.
+
+    Evaluated per (route, expert) on the tokens that chose that expert, with
+    each expert's weights widened to fp64 only while it is in use, so full
+    model sizes (8 x 5632 x 2048 experts) fit in host memory."""
     h, w = _f64(hidden), _f64(routing_weights)
-    g, u, d = _f64(gate_w), _f64(up_w), _f64(down_w)
     sel = selected_experts.detach().cpu().long()
     tokens, top_k = sel.shape
     out = torch.zeros(tokens, h.shape[1], dtype=torch.float64)
-    for j in range(top_k):
-        e = sel[:, j]
-        gate = torch.einsum("tid,td->ti", g[e], h)
-        up = torch.einsum("tid,td->ti", u[e], h)
-        inter = torch.nn.functional.silu(gate) * up
-        y = torch.einsum("tdi,ti->td", d[e], inter)
-        out = out + y * w[:, j : j + 1]
+    experts = gate_w.shape[0]
+    for e in range(experts):
+        hit = sel == e
+        if not bool(hit.any()):
+            continue
+        g, u, d = _f64(gate_w[e]), _f64(up_w[e]), _f64(down_w[e])
+        for j in range(top_k):
+            idx = torch.nonzero(hit[:, j]).reshape(-1)
+            if idx.numel() == 0:
+                continue
+            he = h.index_select(0, idx)
+            inter = torch.nn.functional.silu(he @ g.T) * (he @ u.T)
+            contrib = (inter @ d.T) * w.index_select(0, idx)[:, j : j + 1]
+            out.index_add_(0, idx, contrib)
     return out
 
 

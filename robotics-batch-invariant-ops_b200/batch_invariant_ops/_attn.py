@@ -1,8 +1,11 @@
 """Host side of the fused attention kernels (dense SDPA and varlen).
 
-Both go to one warp-per-query-row kernel (``bio_attention`` /
-``bio_attention_varlen``) that reads Q/K/V through strides, shares KV heads
-for grouped-query attention by index arithmetic and applies masks through
+Both end in one C entry (``bio_attention`` / ``bio_attention_varlen``).
+bf16/fp16 run the tcgen05 kernels: 128-row query tiles (two per CTA for long
+queries) with S and O in TMEM, keys in fixed 128-key blocks, one softmax
+thread per query row; fp32 runs a CUDA-core kernel with one warp per query
+row.  Q/K/V are read through their strides, KV heads are shared for
+grouped-query attention by index arithmetic and masks are applied through
 broadcast strides, so no repeat_interleave, mask materialisation, score
 tensor or host synchronisation is needed.
 """

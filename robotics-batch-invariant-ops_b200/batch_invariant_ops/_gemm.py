@@ -339,6 +339,17 @@ def bmm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tensor:
     return c
 
 
+def tile_for(m: int, n: int, batch: int = 1, sms: int = 148,
+             b_n_contiguous: bool = False) -> tuple[int, int]:
+    """(tile_m, tile_n) that bio_gemm runs for an m x n bf16/fp16 GEMM over
+    ``batch`` products on a device with ``sms`` SMs."""
+    tm, tn = ctypes.c_int32(0), ctypes.c_int32(0)
+    _lib.check(_lib.load().bio_gemm_tile_for(m, n, batch, sms, int(b_n_contiguous),
+                                             ctypes.byref(tm), ctypes.byref(tn)),
+               "bio_gemm_tile_for")
+    return tm.value, tn.value
+
+
 def tile_config(n: int, k: int, dtype: torch.dtype) -> tuple[int, int, int]:
     """(block_m, block_n, block_k) the library uses for (n, k, dtype)."""
     code = _lib.load().bio_gemm_tile_config(n, k, _lib.DTYPE_CODE[dtype])

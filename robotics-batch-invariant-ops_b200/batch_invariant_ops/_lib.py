@@ -89,6 +89,10 @@ SIGNATURES: dict[str, tuple] = {
     "bio_clear_device_status": (ctypes.c_int, [ctypes.c_int]),
     "bio_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P]),
     "bio_gemm_tile_config": (ctypes.c_int, [_I64, _I64, _I32]),
+    "bio_gemm_tile_for": (
+        ctypes.c_int,
+        [_I64, _I64, _I64, _I32, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
+    ),
     "bio_gemm_tiled": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _I32, _I32, _P]),
     "bio_gemm_f32_exact_workspace": (_I64, [ctypes.POINTER(GemmArgs)]),
     "bio_gemm_f32_exact": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _I64, _P]),
@@ -117,6 +121,7 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_I32, _P, _I32, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     ),
+    "bio_selftest_bounded_wait": (ctypes.c_int, [_P, _P, _I64, _I32, _P]),
     "bio_conv_nd_noalloc": (ctypes.c_int, [_I32, _P, _P, _P, _P, _P, _I64, _I32, _P]),
     "bio_pack_rows": (
         ctypes.c_int,

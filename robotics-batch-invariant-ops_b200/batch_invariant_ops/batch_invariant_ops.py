@@ -69,7 +69,8 @@ def _require_cuda(*tensors: torch.Tensor) -> None:
 # GEMM family (reference :271-431, :1600-1620)
 # ---------------------------------------------------------------------------
 def matmul_persistent(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None):
-    """C = a @ b (+ bias) with a schedule fixed by (N, K, dtype) (reference :271-343)."""
+    """C = a @ b (+ bias); every output element is accumulated in a fixed K order
+    that depends on nothing but K and the dtype (reference :271-343)."""
     assert a.shape[1] == b.shape[0], "Incompatible dimensions"
     assert a.dtype == b.dtype, "Incompatible dtypes"
     assert (
@@ -287,7 +288,7 @@ def scaled_dot_product_attention_batch_invariant(
     if query.dtype != key.dtype or query.dtype != value.dtype:
         raise ValueError("query, key, and value must have the same dtype")
     if query.dtype not in {torch.float16, torch.bfloat16, torch.float32}:
-        raise ValueError(f"unsupported varlen attention dtype: {query.dtype}")
+        raise ValueError(f"unsupported attention dtype: {query.dtype}")
     if enable_gqa:
         if query.shape[-3] % key.shape[-3] or key.shape[-3] != value.shape[-3]:
             raise ValueError("invalid grouped-query attention head counts")
@@ -423,7 +424,7 @@ def linalg_vector_norm_batch_invariant(
             torch.float32,
             torch.float64,
         }, f"unsupported dtype: {dtype}"
-        assert dtype != torch.float64, "float64 is not supported by the Triton kernel"
+        assert dtype != torch.float64, "float64 is not supported by the batch-invariant kernels"
         input = input.to(dtype)
     assert input.dtype in _FLOAT_TYPES, f"unsupported dtype: {input.dtype}"
     if dim is None:

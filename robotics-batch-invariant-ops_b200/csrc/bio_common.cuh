@@ -102,9 +102,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Wait for the phase with parity `parity` of `bar` to complete.  Returns false
 // (and sets *abort_flag and the device status) when the wait times out, or
-// when another role of the CTA already aborted.
+// when another role of the CTA already aborted.  `timeout_ns` is the
+// kernels' 2 s everywhere except the wait self-test, which shortens it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* status) {
+                                          volatile int* abort_flag, int* status,
+                                          uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
@@ -112,7 +114,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 63u) == 0u) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
+      if (global_timer_ns() - t0 > timeout_ns) break;
     }
   }
   *abort_flag = 1;
@@ -122,12 +124,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 
 // Wait used only while draining copies at kernel exit: bounded, ignores the
 // abort flag (the copies must land before shared memory is released).
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity,
+                                                uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_u32(bar);
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 0; i < kWaitMaxIters; ++i) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+    if ((i & 63u) == 63u && global_timer_ns() - t0 > timeout_ns) return false;
   }
   return false;
 }

@@ -688,6 +688,30 @@ int64_t dtype_size(int32_t dtype) { return dtype == BIO_F32 ? 4 : 2; }
 
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
+// *acc *= v unless the product leaves [0, 2^62): the scratch bound is the
+// only limit on what the kernels write, so no size may wrap.
+bool mul_in_range(int64_t* acc, int64_t v) {
+  int64_t r = 0;
+  if (v < 0 || __builtin_mul_overflow(*acc, v, &r) || r >= (int64_t{1} << 62)) return false;
+  *acc = r;
+  return true;
+}
+
+// The output extent of every spatial dim must be the one the geometry
+// implies, (in + 2p - d(k-1) - 1) / s + 1 >= 1, with every field below 2^31
+// (so the expression itself cannot overflow).
+bool out_dims_consistent(const bio_conv_geom* g) {
+  constexpr int64_t kLim = int64_t{1} << 31;
+  for (int i = 0; i < 3; ++i) {
+    if (g->in[i] >= kLim || g->kernel[i] >= kLim || g->stride[i] >= kLim ||
+        g->padding[i] >= kLim || g->dilation[i] >= kLim || g->out[i] >= kLim)
+      return false;
+    const int64_t span = g->in[i] + 2 * g->padding[i] - g->dilation[i] * (g->kernel[i] - 1) - 1;
+    if (span < 0 || span / g->stride[i] + 1 != g->out[i]) return false;
+  }
+  return true;
+}
+
 }  // namespace
 
 extern "C" int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* weight,
@@ -696,41 +720,40 @@ extern "C" int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* wei
   if (dtype != BIO_F32 && dtype != BIO_F16 && dtype != BIO_BF16) return BIO_ERR_DTYPE;
   if (!geom_ok(geom) || out_channels < 1 || out_channels % geom->groups != 0)
     return BIO_ERR_SHAPE;
+  if (geom->batch == 0) return BIO_OK;
+  if (!out_dims_consistent(geom)) return BIO_ERR_SHAPE;
   const int64_t groups = geom->groups;
   const int64_t cg = geom->channels / groups;
   const int64_t og = out_channels / groups;
-  const int64_t kvol = geom->kernel[0] * geom->kernel[1] * geom->kernel[2];
-  const int64_t k = cg * kvol;
-  const int64_t kpad = round_up(k, 8);
-  const int64_t L = geom->out[0] * geom->out[1] * geom->out[2];
-  if (geom->batch == 0 || L == 0) return BIO_OK;
-  if (x == nullptr || weight == nullptr || y == nullptr) return BIO_ERR_ARG;
   const int64_t es = dtype_size(dtype);
-  const int64_t patch_bytes = round_up(geom->batch * groups * L * kpad * es, 256);
+  // every size below is checked against wrap-around before it is trusted
+  int64_t k = cg;
+  int64_t L = 1;
+  for (int i = 0; i < 3; ++i)
+    if (!mul_in_range(&k, geom->kernel[i]) || !mul_in_range(&L, geom->out[i]))
+      return BIO_ERR_SCRATCH;
+  const int64_t kpad = round_up(k, 8);
+  int64_t patch_raw = geom->batch;
+  if (!mul_in_range(&patch_raw, groups) || !mul_in_range(&patch_raw, L) ||
+      !mul_in_range(&patch_raw, kpad) || !mul_in_range(&patch_raw, es))
+    return BIO_ERR_SCRATCH;
+  const int64_t patch_bytes = round_up(patch_raw, 256);
+  if (x == nullptr || weight == nullptr || y == nullptr) return BIO_ERR_ARG;
   // the tensor-core GEMM reads the weight with TMA: rows must be 16-byte
   // aligned, otherwise a zero-padded copy goes into the scratch as well
   const bool pack_w = dtype != BIO_F32 &&
                       ((k * es) % 16 != 0 || (reinterpret_cast<uintptr_t>(weight) & 15u) != 0);
-  const int64_t w_bytes = pack_w ? round_up(groups * og * kpad * es, 256) : 0;
-  if (patch_bytes + w_bytes > static_cast<int64_t>(BIO_NOALLOC_SCRATCH_BYTES))
+  int64_t w_raw = pack_w ? groups : 0;
+  if (pack_w && (!mul_in_range(&w_raw, og) || !mul_in_range(&w_raw, kpad) ||
+                 !mul_in_range(&w_raw, es)))
     return BIO_ERR_SCRATCH;
-  int st = bio_host::ensure_device(device);
-  if (st != BIO_OK) return st;
-  unsigned char* scratch = nullptr;
-  st = scratch_address(device, &scratch);
-  if (st != BIO_OK) return st;
+  const int64_t w_bytes = round_up(w_raw, 256);
+  constexpr int64_t kScratch = static_cast<int64_t>(BIO_NOALLOC_SCRATCH_BYTES);
+  if (patch_bytes > kScratch || w_bytes > kScratch - patch_bytes) return BIO_ERR_SCRATCH;
+  const int64_t w_row = pack_w ? kpad : k;
 
-  st = bio_im2col(dtype, x, geom, scratch, kpad, device, stream);
-  if (st != BIO_OK) return st;
-  const void* wa = weight;
-  int64_t w_row = k;
-  if (pack_w) {
-    st = bio_pack_rows(dtype, weight, 1, groups, og, k, 0, og * k, k, 1, scratch + patch_bytes,
-                       kpad, device, stream);
-    if (st != BIO_OK) return st;
-    wa = scratch + patch_bytes;
-    w_row = kpad;
-  }
+  // One GEMM per (sample, group): y[b, g*og + o, l] = W_g[o, :] . patches[b, g, l, :]
+  // (+ bias per output channel), the layout of the regular entry point.
   bio_gemm_args g = {};
   g.dtype = dtype;
   g.flags = BIO_GEMM_BIAS_PER_ROW;
@@ -739,13 +762,11 @@ extern "C" int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* wei
   g.m = og;
   g.n = L;
   g.k = k;
-  g.a = wa;
   g.a_sm = w_row;
   g.a_sk = 1;
   g.a_s1 = 0;
   g.a_s2 = og * w_row;
   g.a_div2 = 1;
-  g.b = scratch;
   g.b_sk = 1;
   g.b_sn = kpad;
   g.b_s1 = groups * L * kpad;
@@ -760,5 +781,28 @@ extern "C" int bio_conv_nd_noalloc(int32_t dtype, const void* x, const void* wei
   g.bias_s2 = og;
   g.alpha = 1.0f;
   g.device = device;
+  // fp32 takes the exact-slice tensor-core GEMM whenever it applies, as the
+  // regular entry point does (same bits); its digit workspace follows the
+  // patches in the array.
+  const int64_t ws_bytes = dtype == BIO_F32 ? bio_gemm_f32_exact_workspace(&g) : 0;
+  if (ws_bytes > kScratch - patch_bytes - w_bytes) return BIO_ERR_SCRATCH;
+
+  int st = bio_host::ensure_device(device);
+  if (st != BIO_OK) return st;
+  unsigned char* scratch = nullptr;
+  st = scratch_address(device, &scratch);
+  if (st != BIO_OK) return st;
+
+  st = bio_im2col(dtype, x, geom, scratch, kpad, device, stream);
+  if (st != BIO_OK) return st;
+  g.a = weight;
+  g.b = scratch;
+  if (pack_w) {
+    st = bio_pack_rows(dtype, weight, 1, groups, og, k, 0, og * k, k, 1, scratch + patch_bytes,
+                       kpad, device, stream);
+    if (st != BIO_OK) return st;
+    g.a = scratch + patch_bytes;
+  }
+  if (ws_bytes > 0) return bio_gemm_f32_exact(&g, scratch + patch_bytes + w_bytes, ws_bytes, stream);
   return bio_gemm(&g, stream);
 }

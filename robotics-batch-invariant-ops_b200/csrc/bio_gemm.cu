@@ -7,14 +7,19 @@
 //               fp32 accumulators in TMEM, double buffered (2 x BN columns).
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, alpha, bias (fp32),
 //               round to the output dtype, store.
-// The tile shape (128 x BN x 64) is a function of (N, K, dtype) only and the
-// K loop always runs k-block 0..K/64-1, MMA-K 16 steps in order, so the bits
-// of output row m depend on row m of A and on B only (never on M, the batch
-// count or the tile a row lands in).  No split-K, no stream-K.
+// The K loop always runs k-block 0..K/64-1, four MMA-K 16 steps per block in
+// order, into one fp32 TMEM accumulator per output element, in every kernel
+// variant; the output tile (CTA pair 256 x 128/256, single CTA 128 x
+// 32..256, chosen from M, N, the batch count and the SM count by pick_tile)
+// only decides which SM computes which elements.  So the bits of output row
+// m depend on row m of A and on B only (never on M, the batch count or the
+// tile a row lands in); tests run every tile on the same inputs and require
+// identical bits.  No split-K, no stream-K.
 //
-// fp32: CUDA-core GEMM (128x128x8 tiles, 8x8 outputs per thread); exact fp64
-// products accumulated with DFMA in sequential k order from k = 0, one final
-// rounding to fp32.
+// fp32 (bio_gemm): CUDA-core GEMM (128x128x8 tiles, 8x8 outputs per thread);
+// exact fp64 products accumulated with DFMA in sequential k order from k = 0,
+// one final rounding to fp32.  (The Python layer sends fp32 with K <= 65536 to
+// the exact-slice int8 tensor-core GEMM of bio_gemm_exact.cu instead.)
 //
 // Reference: matmul_kernel_persistent / bmm_kernel_persistent in
 // batch_invariant_ops/batch_invariant_ops.py:61-229 and their launchers
@@ -1395,6 +1400,14 @@ TileChoice pick_tile(int64_t m, int64_t n, int64_t batch, int sms) {
   return {true, 256};
 }
 
+// The tile bio_gemm runs: pick_tile, widened to one 64-column swizzle atom
+// for an N-contiguous B on the single-CTA path.
+TileChoice run_tile(int64_t m, int64_t n, int64_t batch, int sms, bool b_mn) {
+  TileChoice tc = pick_tile(m, n, batch, sms);
+  if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
+  return tc;
+}
+
 // Configuration reported for (n, k, dtype): the large-M tile and the K block
 // that fixes the accumulation order.
 TileChoice reported_tile(int64_t n) {
@@ -1754,6 +1767,16 @@ int bio_gemm_tile_config(int64_t n, int64_t k, int32_t dtype) {
   return (tc.pair ? 256 : kBM) * 1000000 + tc.bn * 1000 + kBK;
 }
 
+int bio_gemm_tile_for(int64_t m, int64_t n, int64_t batch, int32_t sms, int32_t b_mn,
+                      int32_t* tile_m, int32_t* tile_n) {
+  if (tile_m == nullptr || tile_n == nullptr || m < 1 || n < 1 || batch < 1 || sms < 1)
+    return BIO_ERR_ARG;
+  const TileChoice tc = run_tile(m, n, batch, sms, b_mn != 0);
+  *tile_m = tc.pair ? 256 : kBM;
+  *tile_n = tc.bn;
+  return BIO_OK;
+}
+
 }  // extern "C"
 
 namespace {
@@ -1806,14 +1829,12 @@ int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v) 
   }
   TileChoice tc = forced != nullptr
                      ? *forced
-                     : pick_tile(a->m, a->n, a->batch1 * a->batch2, bio_host::sm_count(a->device));
+                     : run_tile(a->m, a->n, a->batch1 * a->batch2, bio_host::sm_count(a->device),
+                                b_mn);
   if (!tile_supported(tc)) return BIO_ERR_ARG;
   // An N-contiguous B is staged in 64-column swizzle atoms: tiles narrower
   // than one atom are not built for it.
-  if (b_mn && !tc.pair && tc.bn < 64) {
-    if (forced != nullptr) return BIO_ERR_ARG;
-    tc.bn = 64;
-  }
+  if (b_mn && !tc.pair && tc.bn < 64) return BIO_ERR_ARG;
   if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn);
   return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn);
 }

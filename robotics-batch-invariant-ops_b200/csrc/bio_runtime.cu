@@ -83,7 +83,7 @@ const char* bio_status_string(int status) {
     case BIO_ERR_DRIVER: return "CUDA driver entry point or tensor map error";
     case BIO_ERR_ARG: return "invalid argument";
     case BIO_ERR_DEVICE: return "device-side check failed";
-    case BIO_ERR_SCRATCH: return "problem needs more than the fixed no-allocation scratch";
+    case BIO_ERR_SCRATCH: return "scratch or workspace too small for this problem";
     default: return "unknown status";
   }
 }

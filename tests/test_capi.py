@@ -1,6 +1,10 @@
 """CPU checks of the C ABI: the library loads without a GPU and exports every
 function declared in include/bio_sm100.h; the ctypes signature table matches
-the header; the GEMM tile choice depends on (N, K, dtype) only."""
+the header; the K block that fixes every GEMM element's accumulation order
+depends on the dtype only, and the output-tile policy (bio_gemm_tile_for)
+returns only tiles that the library builds (which tile runs is a function of
+m as well: tests/test_gemm_gpu.py runs every such tile on the same inputs and
+requires identical bits)."""
 
 from __future__ import annotations
 
@@ -52,16 +56,41 @@ def test_gemm_args_struct_layout():
 
 @pytest.mark.parametrize("dtype", (torch.float32, torch.float16, torch.bfloat16))
 @pytest.mark.parametrize("n", (1, 91, 4096, 11008, 16384, 184622))
-def test_tile_config_is_a_function_of_n_k_dtype(n, dtype):
+def test_k_block_is_fixed_by_dtype(n, dtype):
     from batch_invariant_ops import _gemm
 
-    cfg = _gemm.tile_config(n, 4096, dtype)
-    assert cfg == _gemm.tile_config(n, 4096, dtype)
-    bm, bn, bk = cfg
+    bm, bn, bk = _gemm.tile_config(n, 4096, dtype)
     if dtype == torch.float32:
         assert (bm, bn, bk) == (128, 128, 8)
     else:
-        assert bm in (128, 256) and bn in (64, 128, 256) and bk == 64
+        assert bk == 64, "the 16-bit K order is 64-wide blocks for every shape"
+        assert bm in (128, 256) and bn in (64, 128, 256)
+
+
+BUILT_TILES = {(128, 32), (128, 64), (128, 128), (128, 256), (256, 128), (256, 256)}
+
+
+@pytest.mark.parametrize("n", (8, 64, 65, 1152, 4096, 11008, 16384, 184622))
+@pytest.mark.parametrize("b_mn", (False, True))
+def test_tile_policy_returns_built_tiles(n, b_mn):
+    from batch_invariant_ops import _gemm
+
+    for m in (1, 8, 32, 127, 128, 129, 256, 400, 512, 1152, 2048, 8192, 65536):
+        for batch in (1, 3, 64):
+            tile = _gemm.tile_for(m, n, batch, 148, b_mn)
+            assert tile in BUILT_TILES, (m, n, batch, tile)
+            if m <= 128:
+                assert tile[0] == 128, "one m-block runs single-CTA tiles"
+            if b_mn and tile[0] == 128:
+                assert tile[1] >= 64, "an N-contiguous B needs a 64-column atom"
+
+
+def test_tile_policy_rejects_bad_arguments():
+    lib = _lib.load()
+    tm, tn = ctypes.c_int32(0), ctypes.c_int32(0)
+    assert lib.bio_gemm_tile_for(0, 8, 1, 148, 0, ctypes.byref(tm), ctypes.byref(tn)) == _lib.BIO_ERR_ARG
+    assert lib.bio_gemm_tile_for(8, 8, 1, 0, 0, ctypes.byref(tm), ctypes.byref(tn)) == _lib.BIO_ERR_ARG
+    assert lib.bio_gemm_tile_for(8, 8, 1, 148, 0, None, ctypes.byref(tn)) == _lib.BIO_ERR_ARG
 
 
 def test_gemm_rejects_bad_arguments_without_gpu():
@@ -114,3 +143,36 @@ def test_struct_layouts_match_the_c_header(tmp_path):
         assert int(got[cname]) == ctypes.sizeof(py), cname
         for fname, _ in py._fields_:
             assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
+
+
+def _noalloc_geom(batch, channels, inp, kernel, out):
+    from batch_invariant_ops import _conv
+
+    return _conv._geom(batch, channels, 1, inp, kernel, (1,) * len(inp), (0,) * len(inp),
+                       (1,) * len(inp), out)
+
+
+def test_noalloc_conv_rejects_sizes_that_would_wrap_without_gpu():
+    """B * G * L * Kpad * dtype bytes would wrap past 2^64 to a small number;
+    the entry point must see the overflow and refuse before touching the GPU
+    (none here: a launch would return BIO_ERR_LAUNCH, not BIO_ERR_SCRATCH)."""
+    lib = _lib.load()
+    geom = _noalloc_geom(2**61, 1, (1, 1), (1, 1), (1, 1))
+    dummy = ctypes.c_void_p(256)
+    rc = lib.bio_conv_nd_noalloc(_lib.BIO_BF16, dummy, dummy, None, dummy, ctypes.byref(geom), 1,
+                                 0, None)
+    assert rc == _lib.BIO_ERR_SCRATCH
+    geom = _noalloc_geom(1, 2**40, (1, 1), (2**12, 2**12), (1, 1))
+    rc = lib.bio_conv_nd_noalloc(_lib.BIO_BF16, dummy, dummy, None, dummy, ctypes.byref(geom), 1,
+                                 0, None)
+    assert rc in (_lib.BIO_ERR_SCRATCH, _lib.BIO_ERR_SHAPE)
+
+
+def test_noalloc_conv_rejects_inconsistent_output_extent_without_gpu():
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(256)
+    # a 3x3 input with a 3x3 kernel gives a 1x1 output, not 2x2
+    geom = _noalloc_geom(1, 4, (3, 3), (3, 3), (2, 2))
+    rc = lib.bio_conv_nd_noalloc(_lib.BIO_BF16, dummy, dummy, None, dummy, ctypes.byref(geom), 8,
+                                 0, None)
+    assert rc == _lib.BIO_ERR_SHAPE

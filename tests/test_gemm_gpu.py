@@ -236,6 +236,32 @@ def test_every_tile_shape_gives_identical_bits(dtype, m, n, k, b_layout, with_bi
     torch.testing.assert_close(ref.double().cpu(), expect, rtol=tol["rtol"], atol=tol["atol"] * scale)
 
 
+@pytest.mark.parametrize("n", (4096, 11008, 16384))
+def test_policy_tiles_at_sweep_switch_points_give_identical_bits(n):
+    """The tile bio_gemm runs depends on M (bio_gemm_tile_for).  For every M of
+    the config-2 sweep and its switch points, collect the tile the policy
+    picks; then run EVERY one of those tiles on the same 8192-row input and
+    require identical bits, and require that the policy's own run at each M
+    gives exactly the rows of the full run."""
+    from batch_invariant_ops import _gemm
+
+    gen = torch.Generator(device="cuda").manual_seed(61_000 + n)
+    k = 4096
+    x = _wide(8192, k, dtype=torch.bfloat16, gen=gen, span=6)
+    w = (torch.randn(n, k, device="cuda", generator=gen) / 64).to(torch.bfloat16)
+    bias = (torch.randn(n, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    ms = (1, 8, 32, 127, 128, 129, 255, 256, 257, 512, 2048, 8192)
+    picked = {m: _gemm.tile_for(m, n, 1, sms) for m in ms}
+    full = linear_batch_invariant(x, w, bias)
+    for tile in sorted(set(picked.values())):
+        out = _gemm.mm(x, w.t(), bias, tile=tile)
+        assert torch.equal(out, full), f"N={n}: tile {tile} differs from the library's run"
+    for m in ms:
+        part = linear_batch_invariant(x[:m], w, bias)
+        assert torch.equal(part, full[:m]), f"N={n}: M={m} (tile {picked[m]}) differs"
+
+
 def test_unsupported_tile_is_rejected():
     from batch_invariant_ops import _gemm
 

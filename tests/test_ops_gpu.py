@@ -322,18 +322,19 @@ def test_sdpa_matches_torch_and_oracle(dtype, causal):
     _close_to_oracle(out, O.sdpa(q, k, v, None, causal), dtype)
 
 
+@pytest.mark.parametrize("dtype", (torch.bfloat16, torch.float16))
 @pytest.mark.parametrize("head_dim", (52, 72, 100))
-def test_sdpa_two_tile_head_dims_below_padded_width(head_dim):
+def test_sdpa_two_tile_head_dims_below_padded_width(head_dim, dtype):
     # more than 128 query rows and equal padded widths take the two-tile kernel;
-    # 52 and 100 end in a partial group of 8 output columns
+    # 52 and 100 end in a partial group of 8 output columns (16-byte stores
+    # for the aligned groups, element stores for the rest, both dtypes)
     gen = torch.Generator(device="cuda").manual_seed(7230 + head_dim)
-    q = _rn(3, 2, 300, head_dim, dtype=torch.bfloat16, gen=gen)
-    k = _rn(3, 2, 300, head_dim, dtype=torch.bfloat16, gen=gen)
-    v = _rn(3, 2, 300, head_dim, dtype=torch.bfloat16, gen=gen)
+    q = _rn(3, 2, 300, head_dim, dtype=dtype, gen=gen)
+    k = _rn(3, 2, 300, head_dim, dtype=dtype, gen=gen)
+    v = _rn(3, 2, 300, head_dim, dtype=dtype, gen=gen)
     out = scaled_dot_product_attention_batch_invariant(q, k, v)
-    torch.testing.assert_close(out, F.scaled_dot_product_attention(q, k, v),
-                               **TOLERANCES[torch.bfloat16])
-    _close_to_oracle(out, O.sdpa(q, k, v, None, False), torch.bfloat16)
+    torch.testing.assert_close(out, F.scaled_dot_product_attention(q, k, v), **TOLERANCES[dtype])
+    _close_to_oracle(out, O.sdpa(q, k, v, None, False), dtype)
     alone = scaled_dot_product_attention_batch_invariant(q[:1], k[:1], v[:1])
     assert_first_sample_equal(alone, out)
 
@@ -461,9 +462,12 @@ def test_moe_is_batch_invariant(dtype):
     together = deterministic_token_choice_moe(hidden, w, sel, gate, up, down)
     assert torch.equal(alone, together[:1])
     ref = O.moe(hidden, w, sel, gate, up, down)
-    tol = {torch.float32: 2e-4, torch.float16: 5e-2, torch.bfloat16: 3e-1}[dtype]
-    err = (together.double().cpu() - ref).abs().max() / ref.abs().max()
-    assert err < tol, err
+    if dtype == torch.float32:
+        err = (together.double().cpu() - ref).abs().max() / ref.abs().max()
+        assert err < 2e-4, err
+    else:  # normwise bar of the 16-bit contract
+        err = (together.double().cpu() - ref).norm() / ref.norm()
+        assert err <= 1e-2, err
 
 
 def test_moe_out_of_range_expert_sets_status_not_trap():

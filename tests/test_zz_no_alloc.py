@@ -10,8 +10,11 @@ alone in a fresh process and after the rest of the suite.
 
 The test calls the entry point through the C ABI (ctypes), twice in a row on
 the same buffers, and compares each result with the regular entry point
-(conv2d/conv3d_batch_invariant: bio_im2col + bio_gemm with PyTorch-allocated
-scratch) within the suite's tolerances.
+(conv2d/conv3d_batch_invariant: bio_im2col + the same GEMM with
+PyTorch-allocated scratch).  Both run the same arithmetic, so the results
+must be identical bit for bit (fp32 included: both take the exact-slice
+GEMM); the first sample run alone must also give the bits it gets in the
+batch.
 """
 
 from __future__ import annotations
@@ -22,7 +25,6 @@ import pytest
 import torch
 
 from batch_invariant_ops import _conv, _lib, conv2d_batch_invariant, conv3d_batch_invariant
-from conftest import TOLERANCES
 
 pytestmark = pytest.mark.gpu
 
@@ -64,14 +66,20 @@ def test_noalloc_conv_matches_regular_entry_point_twice(case):
     b = torch.randn(ws[0], device="cuda", generator=gen).to(dtype)
     fn = conv2d_batch_invariant if kind == "conv2d" else conv3d_batch_invariant
     expected = fn(x, w, b, stride, padding, dilation, False, (0,) * len(stride), groups)
-    tol = {"rtol": 5e-4, "atol": 4e-2} if (kind == "conv3d" and dtype == torch.float32) else TOLERANCES[dtype]
     out = torch.empty_like(expected)
     for _ in range(2):
         out.fill_(float("nan"))
         rc, _ = _noalloc(x, w, b, stride, padding, dilation, groups, out)
         assert rc == _lib.BIO_OK, _lib.status_message(rc)
         torch.cuda.synchronize()
-        torch.testing.assert_close(out, expected, **tol)
+        assert torch.equal(out, expected), (
+            f"max diff {(out.double() - expected.double()).abs().max().item()}")
+    # the first sample alone gives the bits it gets inside the batch
+    alone = torch.full_like(expected[:1], float("nan"))
+    rc, _ = _noalloc(x[:1].contiguous(), w, b, stride, padding, dilation, groups, alone)
+    assert rc == _lib.BIO_OK, _lib.status_message(rc)
+    torch.cuda.synchronize()
+    assert torch.equal(alone, out[:1])
 
 
 def test_noalloc_conv_rejects_problems_beyond_the_scratch():
