@@ -503,8 +503,16 @@ def run_ours(args) -> None:
             line["cpu_fp64_oracle"] = cpu_fp64_oracle(min(5.0, args.cpu_budget))
         if world == 1 and not args.no_triton_ref:
             line["reference_triton_b200"] = _triton_reference(args)
-        print(json.dumps(line), flush=True)
     graphs.clear()
+    del outs
+    torch.cuda.empty_cache()
+    if not args.no_vla:
+        # every rank takes part (sharded step, NCCL gather); rank 0 reports
+        vla = vla_sharded(world, rank, dev, args.vla_global_batch, args.vla_steps, args.warmup)
+        if rank == 0:
+            line["vla"] = vla
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
@@ -791,20 +799,136 @@ def run_ops(args) -> None:
           flush=True)
 
 
+def _vla_inputs(cfg, dev, indices):
+    """Per-global-sample synthetic inputs (image ~ U[0,1], ids uniform over the
+    vocabulary, noise ~ N(0,1)), seeded by the global sample index so that a
+    shard holds exactly the samples the whole batch holds at those rows."""
+    import torch
+
+    imgs, ids, noise = [], [], []
+    for i in indices:
+        g = torch.Generator(device=dev).manual_seed(1000 + i)
+        imgs.append(torch.rand(3, cfg.image_size, cfg.image_size, generator=g, device=dev))
+        ids.append(torch.randint(0, cfg.vocab, (cfg.text_tokens,), generator=g, device=dev))
+        noise.append(torch.randn(cfg.chunk, cfg.action_dim, generator=g, device=dev))
+    return torch.stack(imgs), torch.stack(ids), torch.stack(noise)
+
+
+def vla_sharded(world: int, rank: int, dev, global_batch: int, steps: int, warmup: int) -> dict:
+    """Config 5: the random-init pi0-style VLA step with a fixed global batch
+    sharded contiguously over the ranks (strong scaling, no collective in the
+    step).  Each rank captures its shard's step in a CUDA graph (one capture
+    with set_batch_invariant_mode, one stock), replays it ``steps`` times
+    between CUDA events, and the max over ranks is the step time.  The
+    sharded outputs are then gathered to rank 0 over NCCL and compared bit
+    for bit with rank 0's own run of the whole global batch (and, at one GPU,
+    with a run of the first sample alone).  Returns the record on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    from batch_invariant_ops import set_batch_invariant_mode, sharding
+    from batch_invariant_ops.vla import PiZeroStyleVLA, VLAConfig
+
+    cfg = VLAConfig.full()
+    model = PiZeroStyleVLA(cfg, dev, seed=0).eval()
+    start, end = sharding.shard_range(global_batch, world, rank)
+    imgs, ids, noise = _vla_inputs(cfg, dev, range(start, end))
+    stream = torch.cuda.current_stream(dev)
+
+    def graphed(mode: bool):
+        ctx = set_batch_invariant_mode() if mode else contextlib.nullcontext()
+        with torch.inference_mode(), ctx:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    model(imgs, ids, noise)
+            stream.wait_stream(side)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = model(imgs, ids, noise)
+        return graph, out
+
+    def timed(graph) -> float:
+        for _ in range(max(warmup, 1)):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return sharding.max_over_ranks(e0.elapsed_time(e1) / steps, dev)
+
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    graph, out = graphed(True)
+    ms_mode = timed(graph)
+    clocks = sampler.stop()
+    actions, prefix = out["actions"].clone(), out["prefix"].clone()
+    del graph, out
+    graph, out = graphed(False)
+    ms_stock = timed(graph)
+    del graph, out
+    torch.cuda.empty_cache()
+
+    # verification: gather the shards and compare with one run of the whole batch
+    all_actions = sharding.gather_rows(actions, global_batch)
+    all_prefix = sharding.gather_rows(prefix, global_batch)
+    record = None
+    if rank == 0:
+        with torch.inference_mode(), set_batch_invariant_mode():
+            f_imgs, f_ids, f_noise = _vla_inputs(cfg, dev, range(global_batch))
+            whole = model(f_imgs, f_ids, f_noise)
+            alone = model(f_imgs[:1], f_ids[:1], f_noise[:1])
+        bitwise = bool(torch.equal(all_actions, whole["actions"]) and
+                       torch.equal(all_prefix, whole["prefix"]))
+        first_alone = bool(torch.equal(alone["actions"], whole["actions"][:1]) and
+                           torch.equal(alone["prefix"], whole["prefix"][:1]))
+        per_sample = _vla_flops(cfg)
+        record = {
+            "metric": "pi0-style VLA step samples/s under set_batch_invariant_mode",
+            "value": round(global_batch / (ms_mode * 1e-3), 2),
+            "unit": "samples/s",
+            "n_gpus": world,
+            "scaling": "strong",
+            "global_batch": global_batch,
+            "batch_per_gpu": f"{end - start} (rank 0)",
+            "steps": steps,
+            "ms_per_step": round(ms_mode, 3),
+            "achieved_tflops": round(per_sample * global_batch / (ms_mode * 1e-3) / 1e12, 1),
+            "stock_samples_per_s": round(global_batch / (ms_stock * 1e-3), 2),
+            "stock_ms_per_step": round(ms_stock, 3),
+            "gathered_shards_bitwise_equal_whole_batch_run": bitwise,
+            "first_sample_alone_bitwise_equal": first_alone,
+            "timing": "each rank replays its shard's step from a CUDA graph between CUDA events; "
+                      "max over ranks; stock = the same graph captured with the mode off "
+                      "(cuBLAS, flash attention)",
+            "config": {"workload": "config5-pi0-style-vla", "vision": "27 x 1152 (SigLIP-like)",
+                       "prefix_lm": "18 x 2048, GQA 8/1, head 256, GeGLU 16384",
+                       "action_expert": "18 x 1024, 10 flow steps, chunk 50x32",
+                       "parallelism": f"dp{world} (global batch sharded, no collective in the "
+                                      "step; NCCL gather for verification only)"},
+            "clocks": clocks,
+        }
+    if world > 1:
+        dist.barrier()
+    del model
+    torch.cuda.empty_cache()
+    return record
+
+
 def run_vla(args) -> None:
-    """Config 5: the random-init pi0-style VLA step (vision tower, prefix LM,
-    10 flow steps of the action expert) under set_batch_invariant_mode, the
-    batch sharded across ranks (args.vla_batch samples per rank, weak
-    scaling).  Reports samples/s over all ranks (max-over-ranks device time),
-    the same step with the mode off (stock PyTorch: cuBLAS, flash attention)
-    and a bitwise check that sample 0 alone equals sample 0 in the batch."""
+    """``--vla``: only the config-5 VLA step (see vla_sharded)."""
     import torch
     import torch.distributed as dist
 
     sys.path.insert(0, str(PKG_ROOT))
-    from batch_invariant_ops import set_batch_invariant_mode
-    from batch_invariant_ops.vla import PiZeroStyleVLA, VLAConfig
-
     world, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -812,74 +936,10 @@ def run_vla(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    cfg = VLAConfig.full()
-    model = PiZeroStyleVLA(cfg, dev, seed=0).eval()
-    b = args.vla_batch
-    imgs, ids, noise = [], [], []
-    for i in range(b):  # per global sample index: shards hold different samples
-        g = torch.Generator(device=dev).manual_seed(1000 + rank * b + i)
-        imgs.append(torch.rand(3, cfg.image_size, cfg.image_size, generator=g, device=dev))
-        ids.append(torch.randint(0, cfg.vocab, (cfg.text_tokens,), generator=g, device=dev))
-        noise.append(torch.randn(cfg.chunk, cfg.action_dim, generator=g, device=dev))
-    imgs, ids, noise = torch.stack(imgs), torch.stack(ids), torch.stack(noise)
-    stream = torch.cuda.current_stream(dev)
-
-    def timed(mode: bool) -> float:
-        ctx = set_batch_invariant_mode() if mode else contextlib.nullcontext()
-        with torch.inference_mode(), ctx:
-            for _ in range(args.warmup):
-                model(imgs, ids, noise)
-            if world > 1:
-                dist.barrier()
-            torch.cuda.synchronize(dev)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(args.steps):
-                model(imgs, ids, noise)
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    ms_mode = timed(True)
-    clocks = sampler.stop()
-    ms_stock = timed(False)
-    with torch.inference_mode(), set_batch_invariant_mode():
-        full = model(imgs, ids, noise)
-        alone = model(imgs[:1], ids[:1], noise[:1])
-    exact = all(torch.equal(alone[k], full[k][:1]) for k in ("actions", "prefix"))
-    if world > 1:
-        ok = torch.tensor([1 if exact else 0], device=dev)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-        exact = bool(ok.item())
+    rec = vla_sharded(world, rank, dev, args.vla_global_batch, args.vla_steps, args.warmup)
     if rank == 0:
-        per_sample_flops = _vla_flops(cfg)
-        value = world * b / (ms_mode * 1e-3)
-        print(json.dumps({
-            "metric": "pi0-style VLA step samples/s under set_batch_invariant_mode",
-            "value": round(value, 2), "unit": "samples/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_mode, 3),
-            "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
-            "data": "synthetic (random-init weights, U[0,1] images, random ids, N(0,1) noise)",
-            "config": {"workload": "config5-pi0-style-vla", "batch_per_gpu": b,
-                       "global_batch": world * b, "vision": "27 x 1152 (SigLIP-like)",
-                       "prefix_lm": "18 x 2048, GQA 8/1, head 256, GeGLU 16384",
-                       "action_expert": "18 x 1024, 10 flow steps, chunk 50x32",
-                       "parallelism": f"dp{world} (batch sharded, no collective in the step)"},
-            "achieved_tflops": round(per_sample_flops * world * b / (ms_mode * 1e-3) / 1e12, 1),
-            "stock_samples_per_s": round(world * b / (ms_stock * 1e-3), 2),
-            "stock_ms_per_step": round(ms_stock, 3),
-            "first_sample_bitwise_equal_alone_vs_batch": exact,
-            "clocks": clocks,
-        }), flush=True)
+        print(json.dumps(rec), flush=True)
     if world > 1:
-        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -967,7 +1027,10 @@ def main() -> None:
     parser.add_argument("--ops", action="store_true", help="per-operator roofline table")
     parser.add_argument("--vla", action="store_true",
                         help="config 5: pi0-style VLA step samples/s under the mode")
-    parser.add_argument("--vla-batch", type=int, default=8, help="VLA samples per GPU")
+    parser.add_argument("--vla-global-batch", type=int, default=128,
+                        help="VLA samples per step over all GPUs (sharded)")
+    parser.add_argument("--vla-steps", type=int, default=3, help="timed VLA graph replays")
+    parser.add_argument("--no-vla", action="store_true", help="skip the VLA step in the default run")
     parser.add_argument("--ops-filter", default="", help="only --ops cases whose name has this")
     parser.add_argument("--ops-reference", action="store_true",
                         help="with --ops: time the reference package from baseline/_ref")

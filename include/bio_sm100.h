@@ -228,6 +228,25 @@ BIO_API int bio_reduce(int32_t kind, int32_t dtype_in, int32_t dtype_out, const 
                        void* y, int64_t outer, int64_t n, int64_t inner, int32_t device,
                        void* stream);
 
+#define BIO_NORM_LAYER 0
+#define BIO_NORM_RMS 1
+/* Fused normalisation over the last n elements of each of `rows` rows (row r
+ * of x at x + r * x_row_stride, of y at y + r * y_row_stride, elements
+ * contiguous).  BIO_NORM_LAYER: y = (x - mean) * rsqrt(var + eps) * w + b with
+ * the biased variance; BIO_NORM_RMS: y = x * rsqrt(mean(x^2) + eps) * w (bias
+ * must be NULL).  weight / bias [n] in w_dtype, or NULL (1 / 0).  fp32
+ * arithmetic with a fixed team per row (32 / 256 / 1024 threads by n) and a
+ * fixed fold + xor-shuffle tree, one rounding to dtype; mean_out / rstd_out
+ * (fp32 [rows], optional) receive the row statistics (mean is 0 for RMS).
+ * A row's bits depend on that row and n only.  No counterpart in the
+ * reference, which leaves layer norms to stock torch and builds RMSNorm from
+ * mean_dim (batch_invariant_ops.py:1395-1482); these replace
+ * aten::native_layer_norm and aten::_fused_rms_norm under the mode. */
+BIO_API int bio_norm(int32_t kind, int32_t dtype, int32_t w_dtype, const void* x,
+                     const void* weight, const void* bias, void* y, float* mean_out,
+                     float* rstd_out, int64_t rows, int64_t n, int64_t x_row_stride,
+                     int64_t y_row_stride, float eps, int32_t device, void* stream);
+
 /* ---- convolution lowering -------------------------------------------------
  * Geometry of an N-d convolution, N <= 3, in NC[D][H]W layout; unused
  * leading spatial dims have in = kernel = stride = dilation = out = 1 and

@@ -267,6 +267,38 @@ def vector_norm(x, dims: Sequence[int] | None, keepdim=False):
 
 
 # ---------------------------------------------------------------------------
+# Fused normalisation (additions next to the path: the reference leaves
+# layer norms to stock torch and builds RMSNorm from mean_dim, :1395-1482)
+# ---------------------------------------------------------------------------
+def layer_norm(x, normalized_ndim: int, weight=None, bias=None, eps=1e-5):
+    """(x - mean) / sqrt(var + eps) * weight + bias over the trailing
+    ``normalized_ndim`` dims, biased variance (torch.nn.functional.layer_norm)."""
+    x64 = _f64(x)
+    dims = tuple(range(x64.ndim - normalized_ndim, x64.ndim))
+    mean = x64.mean(dim=dims, keepdim=True)
+    var = ((x64 - mean) ** 2).mean(dim=dims, keepdim=True)
+    out = (x64 - mean) / torch.sqrt(var + eps)
+    if weight is not None:
+        out = out * _f64(weight)
+    if bias is not None:
+        out = out + _f64(bias)
+    return out
+
+
+def rms_norm(x, normalized_ndim: int, weight=None, eps=None):
+    """x / sqrt(mean(x^2) + eps) * weight over the trailing dims
+    (torch.nn.functional.rms_norm; eps defaults to the fp32 epsilon)."""
+    x64 = _f64(x)
+    if eps is None:
+        eps = torch.finfo(torch.float32).eps
+    dims = tuple(range(x64.ndim - normalized_ndim, x64.ndim))
+    out = x64 / torch.sqrt((x64 * x64).mean(dim=dims, keepdim=True) + eps)
+    if weight is not None:
+        out = out * _f64(weight)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Mixture of experts
 # ---------------------------------------------------------------------------
 def moe(hidden, routing_weights, selected_experts, gate_w, up_w, down_w):

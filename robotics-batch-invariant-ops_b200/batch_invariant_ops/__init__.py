@@ -17,11 +17,13 @@ from .batch_invariant_ops import (
     enable_batch_invariant_mode,
     get_batch_invariant_attention_block_size,
     is_batch_invariant_mode_enabled,
+    layer_norm_batch_invariant,
     linalg_vector_norm_batch_invariant,
     linear_batch_invariant,
     log_softmax,
     matmul_persistent,
     mean_dim,
+    rms_norm_batch_invariant,
     scaled_dot_product_attention_batch_invariant,
     set_batch_invariant_mode,
     softmax,
@@ -53,4 +55,7 @@ __all__ = [
     "get_batch_invariant_attention_block_size",
     "AttentionBlockSize",
     "deterministic_token_choice_moe",
+    # additions (no counterpart in the reference): fused normalisations
+    "layer_norm_batch_invariant",
+    "rms_norm_batch_invariant",
 ]

@@ -17,7 +17,7 @@ import math
 
 import torch
 
-from . import _lib
+from . import _lib, tracing
 
 
 class _AttnArgs(ctypes.Structure):
@@ -146,7 +146,16 @@ def sdpa(q, k, v, attn_mask, is_causal, scale):
         mask_keep = me
         a.mask = me.data_ptr()
         a.m_sb, a.m_sh, a.m_sq, a.m_sk = me.stride()
-    _lib.check(_lib.load().bio_attention(ctypes.byref(a), _lib.stream_of(q)), "bio_attention")
+    pushed = tracing.note(
+        "attention", f"bio_attention [B={nb}, H={h}/{hkv}, Lq={lq}, Lk={lk}, D={d}/{dv}, "
+        f"causal={int(bool(is_causal))}]",
+        2.0 * nb * h * lq * lk * (d + dv) / (2 if is_causal else 1),
+        q.element_size() * (q4.numel() + k4.numel() + v4.numel() + out.numel()),
+        q.element_size()) if tracing.active() else False
+    try:
+        _lib.check(_lib.load().bio_attention(ctypes.byref(a), _lib.stream_of(q)), "bio_attention")
+    finally:
+        tracing.done(pushed)
     del mask_keep
     return out.reshape(*lead, h, lq, dv)
 

@@ -25,7 +25,7 @@ import math
 
 import torch
 
-from . import _gemm, _lib
+from . import _gemm, _lib, tracing
 
 
 class _Geom(ctypes.Structure):
@@ -115,26 +115,29 @@ def conv_nd(input, weight, bias, stride, padding, dilation, transposed, output_p
 
     if nd == 1 and groups == channels == cout and weight.shape[1] == 1:
         w = weight.contiguous()
-        _lib.check(
-            lib.bio_depthwise_conv1d(
-                dtype_code,
-                ctypes.c_void_p(x.data_ptr()),
-                ctypes.c_void_p(w.data_ptr()),
-                ctypes.c_void_p(bias_c.data_ptr() if bias_c is not None else 0),
-                ctypes.c_void_p(out.data_ptr()),
-                batch,
-                channels,
-                input.shape[-1],
-                out_shape[0],
-                ksize[0],
-                stride[0],
-                padding[0],
-                dilation[0],
-                dev,
-                stream,
-            ),
-            "bio_depthwise_conv1d",
-        )
+        with tracing.span("conv", f"bio_depthwise_conv1d [B={batch}, C={channels}, L={out_shape[0]}, k={ksize[0]}]",
+                      2.0 * out.numel() * ksize[0],
+                      (x.numel() + out.numel()) * x.element_size(), x.element_size()):
+            _lib.check(
+                lib.bio_depthwise_conv1d(
+                    dtype_code,
+                    ctypes.c_void_p(x.data_ptr()),
+                    ctypes.c_void_p(w.data_ptr()),
+                    ctypes.c_void_p(bias_c.data_ptr() if bias_c is not None else 0),
+                    ctypes.c_void_p(out.data_ptr()),
+                    batch,
+                    channels,
+                    input.shape[-1],
+                    out_shape[0],
+                    ksize[0],
+                    stride[0],
+                    padding[0],
+                    dilation[0],
+                    dev,
+                    stream,
+                ),
+                "bio_depthwise_conv1d",
+            )
         return out
 
     cg = channels // groups
@@ -146,18 +149,20 @@ def conv_nd(input, weight, bias, stride, padding, dilation, transposed, output_p
     patches = torch.empty((batch, groups, lvol, kpad), device=input.device, dtype=input.dtype)
     geom = _geom(batch, channels, groups, input.shape[2:], ksize, stride, padding, dilation,
                  out_shape)
-    _lib.check(
-        lib.bio_im2col(
-            dtype_code,
-            ctypes.c_void_p(x.data_ptr()),
-            ctypes.byref(geom),
-            ctypes.c_void_p(patches.data_ptr()),
-            kpad,
-            dev,
-            stream,
-        ),
-        "bio_im2col",
-    )
+    with tracing.span("conv", f"bio_im2col [B={batch}, G={groups}, L={lvol}, K={k}]", 0,
+                  (x.numel() + patches.numel()) * x.element_size(), x.element_size()):
+        _lib.check(
+            lib.bio_im2col(
+                dtype_code,
+                ctypes.c_void_p(x.data_ptr()),
+                ctypes.byref(geom),
+                ctypes.c_void_p(patches.data_ptr()),
+                kpad,
+                dev,
+                stream,
+            ),
+            "bio_im2col",
+        )
     w = weight.contiguous()
     opa = _gemm.operand_a(w, batch, groups, og, k, k, 1, 0, og * k)
     opb = _gemm.Operand(patches, patches.data_ptr(), 1, kpad, groups * lvol * kpad, lvol * kpad)

@@ -19,7 +19,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _lib
+from . import _lib, tracing
 
 
 def _ceil8(x: int) -> int:
@@ -171,7 +171,29 @@ def operand_b(
     )
 
 
-def launch(
+def launch(a: Operand, b: Operand, c: torch.Tensor, **kw) -> None:
+    """Enqueue one GEMM (see _launch); inside tracing.record_launches the call
+    is recorded with its algorithmic flops and bytes (and an NVTX range)."""
+    pushed = False
+    if tracing.active():
+        m, n, k = kw["m"], kw["n"], kw["k"]
+        b1, b2 = kw["batch1"], kw["batch2"]
+        es = c.element_size()
+        na = (b1 if a.s1 else 1) * (-(-b2 // max(a.div2, 1)) if a.s2 else 1)
+        nb = (b1 if b.s1 else 1) * (-(-b2 // max(b.div2, 1)) if b.s2 else 1)
+        mode = "swiglu" if kw.get("swiglu_up") is not None else (
+            "segmented" if kw.get("segments") is not None else "gemm")
+        pushed = tracing.note(
+            "gemm", f"bio_{mode} [M={m}, N={n}, K={k}, batch={b1 * b2}]",
+            2.0 * m * n * k * b1 * b2 * (2 if mode == "swiglu" else 1),
+            es * (na * m * k + nb * k * n * (2 if mode == "swiglu" else 1) + b1 * b2 * m * n), es)
+    try:
+        _launch(a, b, c, **kw)
+    finally:
+        tracing.done(pushed)
+
+
+def _launch(
     a: Operand,
     b: Operand,
     c: torch.Tensor,

@@ -35,6 +35,9 @@ BIO_DEV_INDEX = 2
 
 BIO_GEMM_BIAS_PER_ROW = 1
 
+BIO_NORM_LAYER = 0
+BIO_NORM_RMS = 1
+
 BIO_F32 = 0
 BIO_F16 = 1
 BIO_BF16 = 2
@@ -100,6 +103,11 @@ SIGNATURES: dict[str, tuple] = {
     "bio_gemm_swiglu": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _P, _P]),
     "bio_softmax": (ctypes.c_int, [_I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "bio_reduce": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _I64, _I64, _I64, _I32, _P]),
+    "bio_norm": (
+        ctypes.c_int,
+        [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _I32,
+         _P],
+    ),
     "bio_im2col": (ctypes.c_int, [_I32, _P, _P, _P, _I64, _I32, _P]),
     "bio_depthwise_conv1d": (
         ctypes.c_int,

@@ -439,6 +439,49 @@ def linalg_vector_norm_batch_invariant(
 
 
 # ---------------------------------------------------------------------------
+# Fused normalisation (not in the reference; see the module docstring)
+# ---------------------------------------------------------------------------
+def layer_norm_batch_invariant(input, normalized_shape, weight=None, bias=None, eps=1e-5):
+    """``F.layer_norm`` with a fixed per-row reduction tree: mean and biased
+    variance in fp32 (two passes over the row in registers), then
+    (x - mean) * rsqrt(var + eps) * weight + bias and one rounding.  The
+    reference leaves layer norms to stock torch; this is the fused kernel
+    its row-reduction design (mean_dim, :1395-1482) implies."""
+    _require_cuda(input, weight, bias)
+    return _rows.norm(input, normalized_shape, weight, bias, eps, rms=False)
+
+
+def rms_norm_batch_invariant(input, normalized_shape, weight=None, eps=None):
+    """``F.rms_norm`` (aten::_fused_rms_norm semantics: fp32 arithmetic,
+    x * rsqrt(mean(x^2) + eps) * weight, one rounding; eps defaults to the
+    fp32 machine epsilon) with a fixed per-row reduction tree.  Replaces the
+    RMSNorm the reference builds from mean_dim (:1395-1482)."""
+    _require_cuda(input, weight)
+    if eps is None:
+        eps = torch.finfo(torch.float32).eps
+    return _rows.norm(input, normalized_shape, weight, None, eps, rms=True)
+
+
+def native_layer_norm_batch_invariant(input, normalized_shape, weight, bias, eps):
+    """``aten::native_layer_norm`` override: (output, mean, rstd), statistics
+    in fp32 with shape input.shape[:-len(normalized_shape)] + (1, ...)."""
+    _require_cuda(input, weight, bias)
+    out, mean, rstd = _rows.norm(input, normalized_shape, weight, bias, eps, rms=False,
+                                 want_stats=True)
+    return out, mean, rstd
+
+
+def fused_rms_norm_batch_invariant(input, normalized_shape, weight, eps):
+    """``aten::_fused_rms_norm`` override: (output, rstd in fp32)."""
+    _require_cuda(input, weight)
+    if eps is None:
+        eps = torch.finfo(torch.float32).eps
+    out, _, rstd = _rows.norm(input, normalized_shape, weight, None, eps, rms=True,
+                              want_stats=True)
+    return out, rstd
+
+
+# ---------------------------------------------------------------------------
 # Mode / dispatcher override (reference :1654-1712)
 # ---------------------------------------------------------------------------
 _batch_invariant_MODE = False
@@ -450,8 +493,10 @@ def is_batch_invariant_mode_enabled():
 
 
 def enable_batch_invariant_mode():
-    """Register the batch-invariant kernels for the 10 aten ops on the current
-    accelerator's dispatch key (reference :1662-1684)."""
+    """Register the batch-invariant kernels for the reference's 10 aten ops on
+    the current accelerator's dispatch key (reference :1662-1684), plus the
+    fused normalisations aten::native_layer_norm and aten::_fused_rms_norm
+    (additions: the reference leaves normalisation to stock torch)."""
     global _batch_invariant_MODE, _batch_invariant_LIB
     if _batch_invariant_MODE:
         return
@@ -474,6 +519,16 @@ def enable_batch_invariant_mode():
     _batch_invariant_LIB.impl(
         "aten::linalg_vector_norm", linalg_vector_norm_batch_invariant, dispatch_key
     )
+    # additions to the reference's 10 overrides: the fused normalisations
+    # (F.layer_norm reaches aten::native_layer_norm, F.rms_norm on CUDA
+    # aten::_fused_rms_norm)
+    _batch_invariant_LIB.impl(
+        "aten::native_layer_norm", native_layer_norm_batch_invariant, dispatch_key
+    )
+    if hasattr(torch.ops.aten, "_fused_rms_norm"):
+        _batch_invariant_LIB.impl(
+            "aten::_fused_rms_norm", fused_rms_norm_batch_invariant, dispatch_key
+        )
 
 
 def disable_batch_invariant_mode():

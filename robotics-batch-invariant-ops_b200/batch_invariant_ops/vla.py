@@ -131,8 +131,9 @@ class PiZeroStyleVLA(torch.nn.Module):
     # ----------------------------------------------------------------- blocks
     @staticmethod
     def _rms(x: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
-        var = x.float().pow(2).mean(-1, keepdim=True)
-        return (x.float() * torch.rsqrt(var + 1e-6)).to(x.dtype) * g
+        # F.rms_norm: one fused kernel (aten::_fused_rms_norm on CUDA, the
+        # library's bio_norm under set_batch_invariant_mode)
+        return F.rms_norm(x, (x.shape[-1],), g, 1e-6)
 
     def _vision(self, images: torch.Tensor) -> torch.Tensor:
         c = self.cfg
@@ -167,6 +168,10 @@ class PiZeroStyleVLA(torch.nn.Module):
         return F.linear(F.gelu(gate, approximate="tanh") * up, w_out)
 
     def _prefix(self, image_tokens, ids):
+        """Prefix LM.  Returns the final hidden state and, per layer, a joint
+        key/value buffer [B, kv_heads, prefix + chunk, head_dim] whose prefix
+        part is filled here; the action expert writes its own keys/values
+        into the tail at every flow step (no concatenation per step)."""
         c = self.cfg
         x = torch.cat([image_tokens, F.embedding(ids, self.embed)], dim=1)
         x = x * math.sqrt(c.lm_width)
@@ -176,7 +181,11 @@ class PiZeroStyleVLA(torch.nn.Module):
         for i in range(c.lm_layers):
             n1, wqkv, wo, n2, w_in, w_out = p[6 * i: 6 * i + 6]
             q, k, v = self._attn_kv(self._rms(x, n1), wqkv, t)
-            kv.append((k, v))
+            kbuf = x.new_empty(b, c.lm_kv_heads, t + c.chunk, c.lm_head_dim)
+            vbuf = torch.empty_like(kbuf)
+            kbuf[:, :, :t] = k
+            vbuf[:, :, :t] = v
+            kv.append((kbuf, vbuf))
             a = F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
             x = x + F.linear(a.transpose(1, 2).reshape(b, t, -1), wo)
             x = x + self._geglu(self._rms(x, n2), w_in, w_out, c.lm_mlp)
@@ -195,9 +204,11 @@ class PiZeroStyleVLA(torch.nn.Module):
         for i in range(c.act_layers):
             n1, wqkv, wo, n2, w_in, w_out = p[6 * i: 6 * i + 6]
             q, k, v = self._attn_kv(self._rms(h, n1), wqkv, c.chunk)
-            kp, vp = kv[i % len(kv)]
-            a = F.scaled_dot_product_attention(q, torch.cat([kp, k], 2), torch.cat([vp, v], 2),
-                                               enable_gqa=True)
+            kbuf, vbuf = kv[i % len(kv)]
+            t_pre = kbuf.shape[2] - c.chunk
+            kbuf[:, :, t_pre:] = k
+            vbuf[:, :, t_pre:] = v
+            a = F.scaled_dot_product_attention(q, kbuf, vbuf, enable_gqa=True)
             h = h + F.linear(a.transpose(1, 2).reshape(b, c.chunk, -1), wo)
             h = h + self._geglu(self._rms(h, n2), w_in, w_out, c.act_mlp)
         return F.linear(self._rms(h, self.act_norm), self.act_out)

@@ -348,32 +348,72 @@ __device__ __forceinline__ void scatter_chunk(const TcGemmParams& p, T* cb, int 
   }
 }
 
+// Bias of an epilogue tile, loaded before the accumulator is ready so that
+// its memory latency overlaps the main loop: lane l holds the column bias of
+// column nbase + 32 c + l in col[c] (0 past N), and the row bias of its own
+// output row m in row (BIAS_PER_ROW, 0 past M).  The scatter mode keeps its
+// own per-channel bias path.
+template <typename T, int NC>
+struct EpiBias {
+  float col[NC];
+  float row;
+  bool has;
+};
+
+template <typename T, int NC>
+__device__ __forceinline__ EpiBias<T, NC> epi_bias_load(const TcGemmParams& p, const T* bias_b,
+                                                       int nbase, int m, int rows, int lane) {
+  EpiBias<T, NC> eb;
+  eb.has = bias_b != nullptr && !p.scatter;
+  eb.row = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) eb.col[c] = 0.f;
+  if (!eb.has) return eb;
+  if (p.bias_per_row) {
+    eb.row = m < rows ? to_f32(bias_b[m]) : 0.f;
+  } else {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int n = nbase + c * 32 + lane;
+      eb.col[c] = n < p.n ? to_f32(bias_b[n]) : 0.f;
+    }
+  }
+  return eb;
+}
+
+// Adds the chunk's bias to v: the row bias, or the 32 column biases taken
+// from the lanes that hold them (every lane of the warp must take part).
+__device__ __forceinline__ void epi_add_bias(float (&v)[32], bool has, bool per_row, float bcol,
+                                             float brow) {
+  if (!has) return;
+  if (per_row) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += brow;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bcol, j);
+  }
+}
+
 // One 32-column chunk of an accumulator row (TMEM words r) of output row m:
 // alpha, then the transposed-convolution scatter, or bias (per column, or
-// per row with BIAS_PER_ROW) and one rounding, 16-byte stores when the row
-// is aligned.  bias already points at this batch's bias vector.
+// per row with BIAS_PER_ROW; prefetched, see EpiBias) and one rounding,
+// 16-byte stores when the row is aligned.  Called by all 32 lanes.  bias
+// points at this batch's bias vector (used by the scatter mode only).
 template <typename T>
 __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const uint32_t (&r)[32], T* crow,
-                                          int m, int rows, int n0, const T* bias) {
-  if (m >= rows || n0 >= p.n) return;
+                                          int m, int rows, int n0, const T* bias, bool has_bias,
+                                          float bcol, float brow) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
   if (p.scatter) {
+    if (m >= rows || n0 >= p.n) return;
     scatter_chunk<T>(p, crow, n0, v, bias);
     return;
   }
-  if (bias != nullptr) {
-    if (p.bias_per_row) {
-      const float bv = to_f32(bias[m]);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += bv;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.n) v[j] += to_f32(bias[n0 + j]);
-    }
-  }
+  epi_add_bias(v, has_bias, p.bias_per_row != 0, bcol, brow);
+  if (m >= rows || n0 >= p.n) return;
   if (p.c_vec_ok && n0 + 32 <= p.n) {
     uint4* dst = reinterpret_cast<uint4*>(crow + n0);
 #pragma unroll
@@ -399,22 +439,12 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const uint32_t 
 // clipped by the tensor store.
 template <typename T>
 __device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uint32_t (&r)[32],
-                                                uint8_t* stage, int m, int n0, const T* bias,
-                                                int lane) {
+                                                uint8_t* stage, bool has_bias, float bcol,
+                                                float brow, int lane) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-  if (bias != nullptr) {
-    if (p.bias_per_row) {
-      const float bv = m < p.m ? to_f32(bias[m]) : 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += bv;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.n) v[j] += to_f32(bias[n0 + j]);
-    }
-  }
+  epi_add_bias(v, has_bias, p.bias_per_row != 0, bcol, brow);
   uint8_t* row = stage + lane * 64;
   const int sw = (lane >> 1) & 3;
 #pragma unroll
@@ -425,6 +455,59 @@ __device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uin
     w.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
     w.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
     *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) = w;
+  }
+}
+
+// Epilogue of one plain (non-SwiGLU) tile for one warp: TMEM columns
+// [0, BN) of its 32 lanes, loaded 32 columns at a time with the next chunk's
+// load in flight while the current one is converted, then stored through
+// the tensor-store staging (c_tma) or directly.  The chunk loop is unrolled
+// so each chunk's prefetched bias sits in a register.
+template <typename T, int BN>
+__device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMap* tmC,
+                                         uint32_t tbase, T* crow, int m, int rows, int nbase,
+                                         const T* bias_b, const EpiBias<T, BN / 32>& eb,
+                                         uint8_t* epi_stage, int q, int lane, int& epi_k,
+                                         int b1, int b2) {
+  const int mrow0 = m - lane;  // first output row of this warp
+  auto emit = [&](const uint32_t(&rr)[32], int c) {
+    const int n0 = nbase + 32 * c;
+    if (p.c_tma) {
+      uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
+      if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+      }
+      epi_chunk_stage<T>(p, rr, buf, eb.has, eb.col[c], eb.row, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (n0 < p.n && mrow0 < p.m) tma_store_4d(tmC, buf, n0, mrow0, b2, b1);
+        bulk_commit();
+      }
+      ++epi_k;
+    } else {
+      epi_chunk<T>(p, rr, crow, m, rows, n0, bias_b, eb.has, eb.col[c], eb.row);
+    }
+  };
+  if constexpr (BN == 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase, r);
+    tmem_ld_wait_tied(r);
+    emit(r, 0);
+  } else {
+    uint32_t ra[32], rb[32];
+    tmem_ld_32x32b_x32(tbase, ra);
+    tmem_ld_wait_tied(ra);
+#pragma unroll
+    for (int c = 0; c < BN / 32; c += 2) {
+      tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 1)), rb);
+      emit(ra, c);
+      tmem_ld_wait_tied(rb);
+      if (c + 2 < BN / 32) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 2)), ra);
+      emit(rb, c + 1);
+      tmem_ld_wait_tied(ra);
+    }
   }
 }
 
@@ -655,61 +738,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
       TileSeg sg;
       const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
+      const int m = ti.mb * kBM + q * 32 + lane;
+      const int nbase = ti.nb * BN;
+      const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+      // bias loads are issued before the wait: their latency overlaps the main loop
+      const EpiBias<T, BN / 32> eb = epi_bias_load<T, BN / 32>(p, bias_b, nbase, m, sg.rows, lane);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const int m = ti.mb * kBM + q * 32 + lane;
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
                 static_cast<int64_t>(sg.base + m) * p.c_sm;
       if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
-{
-        const uint32_t tbase =
-            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-        const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
-        const int nbase = ti.nb * BN;
-        const int mrow0 = m - lane;  // first output row of this warp
-        auto emit = [&](const uint32_t(&rr)[32], int n0) {
-          if (p.c_tma) {
-            uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
-            if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
-              if (lane == 0) bulk_wait_read<1>();
-              __syncwarp();
-            }
-            epi_chunk_stage<T>(p, rr, buf, m, n0, bias_b, lane);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (n0 < p.n && mrow0 < p.m)
-                tma_store_4d(&tmC, buf, n0, mrow0, static_cast<int>(ti.b2),
-                             static_cast<int>(ti.b1));
-              bulk_commit();
-            }
-            ++epi_k;
-          } else {
-            epi_chunk<T>(p, rr, crow, m, sg.rows, n0, bias_b);
-          }
-        };
-        if constexpr (BN == 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase, r);
-          tmem_ld_wait_tied(r);
-          emit(r, nbase);
-        } else {
-          // the next 32 columns load while the current ones are converted
-          uint32_t ra[32], rb[32];
-          tmem_ld_32x32b_x32(tbase, ra);
-          tmem_ld_wait_tied(ra);
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 64) {
-            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 32), rb);
-            emit(ra, nbase + c0);
-            tmem_ld_wait_tied(rb);
-            if (c0 + 64 < BN) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 64), ra);
-            emit(rb, nbase + c0 + 32);
-            tmem_ld_wait_tied(ra);
-          }
-        }
-      }
+      const uint32_t tbase =
+          tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      epi_tile<T, BN>(p, &tmC, tbase, crow, m, sg.rows, nbase, bias_b, eb, epi_stage, q, lane,
+                      epi_k, static_cast<int>(ti.b1), static_cast<int>(ti.b2));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -942,10 +985,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     for (int64_t t = pair; t < total; t += npairs) {
       TileSeg sg;
       const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
+      const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+      // bias loads are issued before the wait: their latency overlaps the main loop
+      const EpiBias<T, BN / 32> eb =
+          p.swiglu ? EpiBias<T, BN / 32>{} : epi_bias_load<T, BN / 32>(p, bias_b, ti.nb * BN, m,
+                                                                    sg.rows, lane);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+
       T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
                 static_cast<int64_t>(sg.base + m) * p.c_sm;
       if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
@@ -993,53 +1042,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         if (acc == 0) acc_phase ^= 1u;
         continue;
       }
-{
+      {
         const uint32_t tbase =
             tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-        const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
-        const int nbase = ti.nb * BN;
-        const int mrow0 = m - lane;  // first output row of this warp
-        auto emit = [&](const uint32_t(&rr)[32], int n0) {
-          if (p.c_tma) {
-            uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
-            if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
-              if (lane == 0) bulk_wait_read<1>();
-              __syncwarp();
-            }
-            epi_chunk_stage<T>(p, rr, buf, m, n0, bias_b, lane);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (n0 < p.n && mrow0 < p.m)
-                tma_store_4d(&tmC, buf, n0, mrow0, static_cast<int>(ti.b2),
-                             static_cast<int>(ti.b1));
-              bulk_commit();
-            }
-            ++epi_k;
-          } else {
-            epi_chunk<T>(p, rr, crow, m, sg.rows, n0, bias_b);
-          }
-        };
-        if constexpr (BN == 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase, r);
-          tmem_ld_wait_tied(r);
-          emit(r, nbase);
-        } else {
-          // the next 32 columns load while the current ones are converted
-          uint32_t ra[32], rb[32];
-          tmem_ld_32x32b_x32(tbase, ra);
-          tmem_ld_wait_tied(ra);
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 64) {
-            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 32), rb);
-            emit(ra, nbase + c0);
-            tmem_ld_wait_tied(rb);
-            if (c0 + 64 < BN) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0 + 64), ra);
-            emit(rb, nbase + c0 + 32);
-            tmem_ld_wait_tied(ra);
-          }
-        }
+        epi_tile<T, BN>(p, &tmC, tbase, crow, m, sg.rows, ti.nb * BN, bias_b, eb, epi_stage, q,
+                        lane, epi_k, static_cast<int>(ti.b1), static_cast<int>(ti.b2));
       }
       tc_fence_before();
       __syncwarp();

