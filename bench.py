@@ -923,6 +923,152 @@ def vla_sharded(world: int, rank: int, dev, global_batch: int, steps: int, warmu
     return record
 
 
+def _extended_cases(dev):
+    """(id, kind, ours, stock) for the 54 extended shapes of
+    tests/golden/extended_shapes.json (the operator shapes the reference
+    benchmarked on real VLA models, research/*/benchmarks.json), with inputs
+    built as in tests/test_extended_shapes_gpu.py; stock is the plain torch
+    op (None where torch has no direct counterpart: varlen, MoE)."""
+    import zlib
+
+    import torch
+    import torch.nn.functional as F
+
+    import batch_invariant_ops as bio
+    from batch_invariant_ops.batch_invariant_ops import addmm_batch_invariant, mm_batch_invariant
+
+    dt = {"torch.bfloat16": torch.bfloat16, "torch.float16": torch.float16,
+          "torch.float32": torch.float32}
+    cases = json.loads((ROOT / "tests" / "golden" / "extended_shapes.json").read_text())["cases"]
+    for case in cases:
+        kind, sh = case["kind"], case["shape"]
+        dtype = dt[sh["dtype"]]
+        gen = torch.Generator(device=dev).manual_seed(zlib.crc32(case["id"].encode()))
+
+        def rnd(shape, scale=1.0):
+            return (torch.randn(*shape, device=dev, generator=gen) * scale).to(dtype)
+
+        ours = stock = None
+        if kind in ("mm", "addmm"):
+            a, b = rnd(sh["left"]), rnd(sh["right"], sh["right"][-2] ** -0.5)
+            if a.ndim == 3:
+                b = b[: a.shape[0]] if b.ndim == 3 else b
+                ours = lambda a=a, b=b: bio.bmm_persistent(a, b)  # noqa: E731
+                stock = lambda a=a, b=b: torch.bmm(a, b)  # noqa: E731
+            elif kind == "addmm":
+                bias = rnd(sh["bias"], 0.1)
+                ours = lambda a=a, b=b, c=bias: addmm_batch_invariant(c, a, b)  # noqa: E731
+                stock = lambda a=a, b=b, c=bias: torch.addmm(c, a, b)  # noqa: E731
+            else:
+                ours = lambda a=a, b=b: mm_batch_invariant(a, b)  # noqa: E731
+                stock = lambda a=a, b=b: torch.mm(a, b)  # noqa: E731
+        elif kind == "linear":
+            x, w = rnd(sh["input"]), rnd(sh["weight"], sh["weight"][1] ** -0.5)
+            b = rnd(sh["bias"], 0.1) if sh.get("bias") else None
+            ours = lambda x=x, w=w, b=b: bio.linear_batch_invariant(x, w, b)  # noqa: E731
+            stock = lambda x=x, w=w, b=b: F.linear(x, w, b)  # noqa: E731
+        elif kind == "sdpa":
+            q, k, v = rnd(sh["query"]), rnd(sh["key"]), rnd(sh["value"])
+            gqa, causal = q.shape[1] != k.shape[1], bool(sh["causal"])
+            ours = lambda q=q, k=k, v=v: bio.scaled_dot_product_attention_batch_invariant(  # noqa: E731
+                q, k, v, is_causal=causal, enable_gqa=gqa)
+            stock = lambda q=q, k=k, v=v: F.scaled_dot_product_attention(  # noqa: E731
+                q, k, v, is_causal=causal, enable_gqa=gqa)
+        elif kind == "varlen":
+            lq, lk = sh["logical_query_length"], sh["logical_kv_length"]
+            nseq = max(2, sh["query"][1] // lq)
+            q = rnd((1, nseq * lq, sh["query_heads"], sh["head_dim"]))
+            k = rnd((1, nseq * lk, sh["kv_heads"], sh["head_dim"]))
+            v = rnd((1, nseq * lk, sh["kv_heads"], sh["head_dim"]))
+            cq = torch.arange(nseq + 1, device=dev, dtype=torch.int32) * lq
+            ck = torch.arange(nseq + 1, device=dev, dtype=torch.int32) * lk
+            ours = lambda q=q, k=k, v=v, cq=cq, ck=ck: (  # noqa: E731
+                bio.varlen_scaled_dot_product_attention_batch_invariant(
+                    q, k, v, cq, ck, is_causal=bool(sh["causal"])))
+        elif kind in ("conv", "depthwise_conv1d", "conv_transpose"):
+            x, w = rnd(sh["input"]), rnd(sh["weight"], 0.05)
+            b = rnd(sh["bias"], 0.1) if sh.get("bias") else None
+            nd = x.ndim - 2
+            stride = tuple(sh.get("stride", [1] * nd))
+            padding = tuple(sh.get("padding", [0] * nd))
+            groups = int(sh.get("groups", 1))
+            if kind == "conv_transpose":
+                fn = {2: bio.conv_transpose2d_batch_invariant, 3: bio.conv_transpose3d_batch_invariant}[nd]
+                tfn = {2: F.conv_transpose2d, 3: F.conv_transpose3d}[nd]
+                ours = lambda x=x, w=w, b=b: fn(x, w, b, stride, padding, (1,) * nd, (0,) * nd,  # noqa: E731
+                                                groups)
+            else:
+                fn = {1: bio.conv1d_batch_invariant, 2: bio.conv2d_batch_invariant,
+                      3: bio.conv3d_batch_invariant}[nd]
+                tfn = {1: F.conv1d, 2: F.conv2d, 3: F.conv3d}[nd]
+                ours = lambda x=x, w=w, b=b: fn(x, w, b, stride, padding, (1,) * nd, False,  # noqa: E731
+                                                (0,) * nd, groups)
+            stock = lambda x=x, w=w, b=b: tfn(x, w, b, stride=stride, padding=padding,  # noqa: E731
+                                              groups=groups)
+        elif kind == "mean":
+            x = rnd(sh["input"])
+            dim = sh.get("dimension", sh.get("dim"))
+            keep = bool(sh.get("keepdim", False))
+            ours = lambda x=x: bio.mean_dim(x, dim, keep)  # noqa: E731
+            stock = lambda x=x: x.mean(dim, keepdim=keep)  # noqa: E731
+        elif kind == "vector_norm":
+            x = rnd(sh["input"])
+            ours = lambda x=x: bio.linalg_vector_norm_batch_invariant(x, dim=sh["dim"])  # noqa: E731
+            stock = lambda x=x: torch.linalg.vector_norm(x, dim=sh["dim"])  # noqa: E731
+        elif kind == "moe":
+            t, dmodel = sh["hidden"]
+            e, topk, inter = sh["experts"], sh["top_k"], sh["intermediate"]
+            hid = rnd((t, dmodel))
+            gate, up = rnd((e, inter, dmodel), 0.02), rnd((e, inter, dmodel), 0.02)
+            down = rnd((e, dmodel, inter), 0.02)
+            logits = torch.randn(t, e, device=dev, generator=gen)
+            top, sel = torch.topk(logits, topk)
+            rw = torch.softmax(top, -1).to(dtype)
+            ours = lambda: bio.deterministic_token_choice_moe(hid, rw, sel, gate, up, down)  # noqa: E731
+        yield case["id"], kind, sh["dtype"].split(".")[-1], ours, stock
+
+
+def run_extended(args) -> None:
+    """``--extended``: time every extended shape (ours and stock torch, L2
+    flushed before each call, CUDA events, median of 5) with the call's
+    algorithmic flops / bytes from the library's launch records and the
+    roofline fraction against MEASURED_PEAKS.json; the per-model benchmark
+    pattern of the reference (scripts/benchmark_batch_invariant_ops.py)."""
+    import torch
+
+    from batch_invariant_ops import tracing
+
+    dev = torch.device("cuda", 0)
+    flush = _Flusher(dev)
+    peaks, _ = _peaks()
+    rows = []
+    for cid, kind, dtype, ours, stock in _extended_cases(dev):
+        ours()
+        torch.cuda.synchronize()
+        with tracing.record_launches() as rec:
+            ours()
+        flops = sum(next((v for k, v in r.items() if k.startswith("flops")), 0.0) for r in rec)
+        nbytes = sum(r["bytes"] for r in rec)
+        t = _time_op(ours, flush)
+        row = {"id": cid, "kind": kind, "dtype": dtype, "us": round(t * 1e6, 1),
+               "launches": len(rec)}
+        if flops:
+            row["tflops"] = round(flops / t / 1e12, 1)
+        row["gbs"] = round(nbytes / t / 1e9, 1)
+        tensor_peak = peaks["bf16_tflops"] if dtype != "float32" else None
+        if flops and tensor_peak and flops / max(nbytes, 1) >= tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9):
+            row["bound"], row["frac"] = "tensor", round(flops / t / 1e12 / tensor_peak, 3)
+        else:
+            row["bound"], row["frac"] = "hbm", round(nbytes / t / 1e9 / peaks["hbm_gbs"], 3)
+        if stock is not None:
+            ts = _time_op(stock, flush)
+            row["stock_us"] = round(ts * 1e6, 1)
+            row["speedup_vs_stock"] = round(ts / t, 3)
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+    print(json.dumps({"extended": len(rows), "impl": "ours"}), flush=True)
+
+
 def run_vla(args) -> None:
     """``--vla``: only the config-5 VLA step (see vla_sharded)."""
     import torch
@@ -1025,6 +1171,8 @@ def main() -> None:
     parser.add_argument("--triton-ref-worker", action="store_true", help=argparse.SUPPRESS)
     parser.add_argument("--profile-point", default=None, help="MxN: run one GEMM point (for ncu)")
     parser.add_argument("--ops", action="store_true", help="per-operator roofline table")
+    parser.add_argument("--extended", action="store_true",
+                        help="time the 54 extended VLA operator shapes (ours vs stock)")
     parser.add_argument("--vla", action="store_true",
                         help="config 5: pi0-style VLA step samples/s under the mode")
     parser.add_argument("--vla-global-batch", type=int, default=128,
@@ -1037,6 +1185,9 @@ def main() -> None:
     args = parser.parse_args()
     if args.vla:
         run_vla(args)
+    elif args.extended:
+        sys.path.insert(0, str(PKG_ROOT))
+        run_extended(args)
     elif args.ops:
         run_ops(args)
     elif args.profile_point:
