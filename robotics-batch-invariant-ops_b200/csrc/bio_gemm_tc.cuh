@@ -1,0 +1,1537 @@
+// Tensor-core GEMM kernels of bio_gemm.cu (bf16 / fp16) and their host
+// launcher: tensor maps, tile policy and the per-layout dispatch.
+// Included by bio_gemm.cu (entry points) and by the bio_gemm_tc_*.cu
+// translation units, each of which instantiates the kernels of one
+// (A layout, B layout, dtype).
+#pragma once
+
+#include <mutex>
+
+#include "bio_common.cuh"
+
+namespace bio {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+struct TcGemmParams {
+  int m, n, k;
+  int tiles_m, tiles_n, k_blocks, group_m;
+  // paired kernel: runtime ring depth, byte stride between A stages and the
+  // row count of the tail box (valid rows of a partial 128-row A slab,
+  // rounded up to 8); 0 when M is a multiple of 128.
+  int stages, a_stride, a_tail_rows;
+  // single-CTA kernel: k-blocks moved per tensor copy (1, or 2/4/8 with the
+  // K-chunked 5-D maps); the ring is grouped in runs of kchunk slots
+  int kchunk;
+  // segmented GEMM (seg != nullptr): segment s owns A/C rows
+  // [seg[s], seg[s+1]) and B batch s; nseg segments, batch2 == 1.  Every CTA
+  // builds a table of m-tiles per segment at start, so tiles are only ever
+  // issued for rows that exist and the tile count needs no host sync.
+  const int* seg;
+  int nseg;
+  // SwiGLU mode (CTA pair, BN = 256): the leader CTA's half of the B tile
+  // comes from tmB (gate) and the peer's from tmB2 (up) at the same rows, so
+  // accumulator columns [0, 128) hold gate and [128, 256) up for 128 output
+  // columns; the epilogue stores round(silu(round(gate)) * round(up)).
+  int swiglu;
+  // Transposed-convolution scatter (stride == kernel): tile row m is input
+  // position (s0, s1, s2), column n is (o, t0, t1, t2); the element is
+  // rounded, gets + bias[o] (bias added after rounding, as the reference's
+  // output + bias), and is stored at c + b1*c_s1 + b2*c_s2 + row_off(m) +
+  // col_off(n).  sc_vec: runs of k2 outputs are stored as one vector.
+  int scatter;
+  int sc_s1, sc_s2, sc_k0, sc_k1, sc_k2, sc_kvol, sc_o2, sc_vec;
+  // plain mode: each epilogue warp stages its 32 x 32 output chunks in
+  // shared memory (64-byte swizzle) and writes them with tensor stores
+  int c_tma;
+  int64_t sc_so, sc_o1o2;
+  int64_t batch2;
+  int64_t total_tiles;
+  int a_div2, b_div2;
+  int a_bcast1, a_bcast2, b_bcast1, b_bcast2;
+  void* c;
+  int64_t c_sm, c_sn, c_s1, c_s2;
+  const void* bias;
+  int64_t bias_s2;
+  int bias_per_row;
+  float alpha;
+  int c_vec_ok;
+  int* status;
+};
+
+struct TileIdx {
+  int64_t b1, b2;
+  int mb, nb;
+};
+
+// Tile t -> (batch, m-block, n-block).  Grouped raster: a group of `group_m`
+// m-blocks (sized on the host so the group's A panel stays in L2) sweeps all
+// n-blocks, so each B panel is streamed once per group.  The order only
+// decides which CTA computes a tile, never the arithmetic of the tile.
+__device__ __forceinline__ TileIdx decode_tile(int64_t t, int tiles_m, int tiles_n,
+                                               int64_t batch2, int group_m) {
+  const int64_t per = static_cast<int64_t>(tiles_m) * tiles_n;
+  const int64_t bi = t / per;
+  const int r = static_cast<int>(t - bi * per);
+  const int in_group = group_m * tiles_n;
+  const int g = r / in_group;
+  const int first_m = g * group_m;
+  const int gsz = min(tiles_m - first_m, group_m);
+  const int rr = r - g * in_group;
+  TileIdx ti;
+  ti.mb = first_m + rr % gsz;
+  ti.nb = rr / gsz;
+  ti.b1 = bi / batch2;
+  ti.b2 = bi - ti.b1 * batch2;
+  return ti;
+}
+
+// Segmented GEMMs: at most kMaxSegs segments.  Each CTA keeps the offsets
+// and an exclusive prefix of m-tiles per segment in shared memory.
+constexpr int kMaxSegs = 1024;
+constexpr uint32_t kSegBytes = 2 * (kMaxSegs + 1) * 4;
+// Epilogue staging for tensor stores: 4 warps x 2 buffers x (32 rows x 64 B).
+constexpr uint32_t kEpiBytes = 4 * 2 * 2048;
+
+struct TileSeg {
+  int base, rows;  // first A/C row of the tile's segment and its row count
+};
+
+// Build the segment table (one warp).  A segment whose offsets are out of
+// order or outside [0, m] gets no tiles and raises BIO_DEV_INDEX.
+__device__ __forceinline__ void seg_table_build(const TcGemmParams& p, int tile_m, int* seg_off,
+                                                int* seg_tiles, int lane) {
+  const int ns = p.nseg;
+  const int per = (ns + 31) / 32;
+  const int s0 = min(lane * per, ns);
+  const int s1 = min(s0 + per, ns);
+  int sum = 0;
+  bool bad = false;
+  for (int s = s0; s < s1; ++s) {
+    const int lo = p.seg[s];
+    const int hi = p.seg[s + 1];
+    const bool ok = lo >= 0 && lo <= hi && hi <= p.m;
+    bad |= !ok;
+    const int cnt = ok ? (hi - lo + tile_m - 1) / tile_m : 0;
+    seg_off[s] = lo;
+    seg_tiles[s] = cnt;
+    sum += cnt;
+  }
+  if (lane == 0) seg_off[ns] = p.seg[ns];
+  int incl = sum;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  int run = incl - sum;
+  for (int s = s0; s < s1; ++s) {
+    const int cnt = seg_tiles[s];
+    seg_tiles[s] = run;
+    run += cnt;
+  }
+  if (lane == 31) seg_tiles[ns] = incl;
+  if (__any_sync(0xffffffffu, bad) && lane == 0) raise_status(p.status, BIO_DEV_INDEX);
+}
+
+// Tiles of the launch: the host count, or (segmented) m-tiles x n-tiles from
+// the shared table.
+__device__ __forceinline__ int64_t tile_total(const TcGemmParams& p, const int* seg_tiles) {
+  return p.seg != nullptr ? static_cast<int64_t>(seg_tiles[p.nseg]) * p.tiles_n : p.total_tiles;
+}
+
+// Tile t -> indices and its segment.  Segmented: the raster runs over the
+// concatenated m-tiles of all segments; a binary search over the prefix
+// finds the segment (empty segments have equal prefix entries and are
+// never chosen) and the m-block within it.
+__device__ __forceinline__ TileIdx tile_at(int64_t t, const TcGemmParams& p, const int* seg_off,
+                                           const int* seg_tiles, TileSeg* sg) {
+  if (p.seg == nullptr) {
+    sg->base = 0;
+    sg->rows = p.m;
+    return decode_tile(t, p.tiles_m, p.tiles_n, p.batch2, p.group_m);
+  }
+  TileIdx ti = decode_tile(t, seg_tiles[p.nseg], p.tiles_n, 1, p.group_m);
+  int lo = 0, hi = p.nseg;  // seg_tiles[lo] <= mb < seg_tiles[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (seg_tiles[mid] <= ti.mb)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  ti.mb -= seg_tiles[lo];
+  ti.b1 = lo;
+  sg->base = seg_off[lo];
+  sg->rows = seg_off[lo + 1] - seg_off[lo];
+  return ti;
+}
+
+// Rows of a segment slab: any row makes the whole 128-row slab load (rows
+// past the segment only feed outputs that are not stored).
+__device__ __forceinline__ int seg_valid(const TcGemmParams& p, int v) {
+  return (p.seg != nullptr && v > 0 && v < 128) ? 128 : v;
+}
+
+template <typename T>
+struct TypeFmt;
+template <>
+struct TypeFmt<__half> {
+  static constexpr uint32_t umma = 0;
+};
+template <>
+struct TypeFmt<__nv_bfloat16> {
+  static constexpr uint32_t umma = 1;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// ---- transposed-convolution scatter epilogue
+__device__ __forceinline__ int64_t scatter_row_off(const TcGemmParams& p, int m) {
+  const int s2 = m % p.sc_s2;
+  const int r = m / p.sc_s2;
+  const int s1 = r % p.sc_s1;
+  const int s0 = r / p.sc_s1;
+  return static_cast<int64_t>(s0) * p.sc_k0 * p.sc_o1o2 +
+         static_cast<int64_t>(s1) * p.sc_k1 * p.sc_o2 + static_cast<int64_t>(s2) * p.sc_k2;
+}
+
+__device__ __forceinline__ int64_t scatter_col_off(const TcGemmParams& p, int n, int* o) {
+  const int oc = n / p.sc_kvol;
+  const int rem = n - oc * p.sc_kvol;
+  const int k12 = p.sc_k1 * p.sc_k2;
+  const int t0 = rem / k12;
+  const int rem2 = rem - t0 * k12;
+  const int t1 = rem2 / p.sc_k2;
+  const int t2 = rem2 - t1 * p.sc_k2;
+  *o = oc;
+  return static_cast<int64_t>(oc) * p.sc_so + static_cast<int64_t>(t0) * p.sc_o1o2 +
+         static_cast<int64_t>(t1) * p.sc_o2 + t2;
+}
+
+template <typename T>
+__device__ __forceinline__ float scatter_value(float v, const T* bias, int o) {
+  const float x = round_to<T>(v);
+  return bias != nullptr ? x + to_f32(bias[o]) : x;
+}
+
+// K2 contiguous outputs (one kernel row) from v[0 .. K2): pairs rounded with
+// one packed conversion; with a bias, the rounded pair is widened, the bias
+// added in fp32 and the sum rounded again (the reference's output + bias).
+template <typename T>
+__device__ __forceinline__ uint32_t scatter_pair(float lo, float hi, bool has_bias, float bv) {
+  uint32_t w = pack2<T>(lo, hi);
+  if (has_bias) {
+    const T* e = reinterpret_cast<const T*>(&w);
+    w = pack2<T>(to_f32(e[0]) + bv, to_f32(e[1]) + bv);
+  }
+  return w;
+}
+
+template <typename T, int K2>
+__device__ __forceinline__ void store_run(T* dst, const float* v, const T* bias, int o, bool vec) {
+  const bool hb = bias != nullptr;
+  const float bv = hb ? to_f32(bias[o]) : 0.f;
+  if constexpr (K2 == 1) {
+    dst[0] = from_f32<T>(scatter_value<T>(v[0], bias, o));
+  } else {
+    uint32_t w[K2 / 2];
+#pragma unroll
+    for (int i = 0; i < K2 / 2; ++i) w[i] = scatter_pair<T>(v[2 * i], v[2 * i + 1], hb, bv);
+    constexpr int kBytes = K2 * static_cast<int>(sizeof(T));
+    if (vec) {
+      if constexpr (kBytes == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = w[0];
+      } else if constexpr (kBytes == 8) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kBytes / 16; ++q)
+          reinterpret_cast<uint4*>(dst)[q] =
+              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < K2 / 2; ++i) {
+        const T* e = reinterpret_cast<const T*>(&w[i]);
+        dst[2 * i] = e[0];
+        dst[2 * i + 1] = e[1];
+      }
+    }
+  }
+}
+
+// Runs of K2 (a divisor of 32) outputs: the chunk start n0 (a multiple of
+// 32) begins a kernel row (t2 = 0); later runs step (t1, t0, o) without
+// divisions.
+template <typename T, int K2>
+__device__ __forceinline__ void scatter_runs(const TcGemmParams& p, T* cb, int n0,
+                                             const float (&v)[32], const T* bias) {
+  int o;
+  scatter_col_off(p, n0, &o);
+  const int k12 = p.sc_k1 * p.sc_k2;
+  const int rem = n0 - o * p.sc_kvol;
+  int t0 = rem / k12;
+  int t1 = (rem - t0 * k12) / K2;
+#pragma unroll
+  for (int r = 0; r < 32; r += K2) {
+    if (n0 + r < p.n) {  // n is a multiple of k2: runs are whole
+      const int64_t off = static_cast<int64_t>(o) * p.sc_so +
+                          static_cast<int64_t>(t0) * p.sc_o1o2 +
+                          static_cast<int64_t>(t1) * p.sc_o2;
+      store_run<T, K2>(cb + off, v + r, bias, o, p.sc_vec != 0);
+    }
+    if (++t1 == p.sc_k1) {
+      t1 = 0;
+      if (++t0 == p.sc_k0) {
+        t0 = 0;
+        ++o;
+      }
+    }
+  }
+}
+
+// One 32-column chunk of a scatter tile row (cb already holds the row's
+// offset and the batch bases; bias points at this group's channels).
+template <typename T>
+__device__ __forceinline__ void scatter_chunk(const TcGemmParams& p, T* cb, int n0,
+                                              const float (&v)[32], const T* bias) {
+  switch (p.sc_k2) {
+    case 1: scatter_runs<T, 1>(p, cb, n0, v, bias); break;
+    case 2: scatter_runs<T, 2>(p, cb, n0, v, bias); break;
+    case 4: scatter_runs<T, 4>(p, cb, n0, v, bias); break;
+    case 8: scatter_runs<T, 8>(p, cb, n0, v, bias); break;
+    case 16: scatter_runs<T, 16>(p, cb, n0, v, bias); break;
+    case 32: scatter_runs<T, 32>(p, cb, n0, v, bias); break;
+    default:
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (n0 + j < p.n) {
+          int o;
+          const int64_t off = scatter_col_off(p, n0 + j, &o);
+          cb[off] = from_f32<T>(scatter_value<T>(v[j], bias, o));
+        }
+      }
+      break;
+  }
+}
+
+// Bias of an epilogue tile, loaded before the accumulator is ready so that
+// its memory latency overlaps the main loop: lane l holds the column bias of
+// column nbase + 32 c + l in col[c] (0 past N), and the row bias of its own
+// output row m in row (BIAS_PER_ROW, 0 past M).  The scatter mode keeps its
+// own per-channel bias path.
+template <typename T, int NC>
+struct EpiBias {
+  float col[NC];
+  float row;
+  bool has;
+};
+
+template <typename T, int NC>
+__device__ __forceinline__ EpiBias<T, NC> epi_bias_load(const TcGemmParams& p, const T* bias_b,
+                                                       int nbase, int m, int rows, int lane) {
+  EpiBias<T, NC> eb;
+  eb.has = bias_b != nullptr && !p.scatter;
+  eb.row = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) eb.col[c] = 0.f;
+  if (!eb.has) return eb;
+  if (p.bias_per_row) {
+    eb.row = m < rows ? to_f32(bias_b[m]) : 0.f;
+  } else {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int n = nbase + c * 32 + lane;
+      eb.col[c] = n < p.n ? to_f32(bias_b[n]) : 0.f;
+    }
+  }
+  return eb;
+}
+
+// Adds the chunk's bias to v: the row bias, or the 32 column biases taken
+// from the lanes that hold them (every lane of the warp must take part).
+__device__ __forceinline__ void epi_add_bias(float (&v)[32], bool has, bool per_row, float bcol,
+                                             float brow) {
+  if (!has) return;
+  if (per_row) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += brow;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bcol, j);
+  }
+}
+
+// One 32-column chunk of an accumulator row (TMEM words r) of output row m:
+// alpha, then the transposed-convolution scatter, or bias (per column, or
+// per row with BIAS_PER_ROW; prefetched, see EpiBias) and one rounding,
+// 16-byte stores when the row is aligned.  Called by all 32 lanes.  bias
+// points at this batch's bias vector (used by the scatter mode only).
+template <typename T>
+__device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const uint32_t (&r)[32], T* crow,
+                                          int m, int rows, int n0, const T* bias, bool has_bias,
+                                          float bcol, float brow) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  if (p.scatter) {
+    if (m >= rows || n0 >= p.n) return;
+    scatter_chunk<T>(p, crow, n0, v, bias);
+    return;
+  }
+  epi_add_bias(v, has_bias, p.bias_per_row != 0, bcol, brow);
+  if (m >= rows || n0 >= p.n) return;
+  if (p.c_vec_ok && n0 + 32 <= p.n) {
+    uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+      dst[j] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+  }
+}
+
+// Tensor-store form of epi_chunk (plain mode, 16-bit C, no scatter): lane l
+// writes its 32 outputs (64 bytes) as row l of a 32 x 32 staging box with the
+// 64-byte swizzle (16-byte chunk c of row l at chunk c ^ ((l >> 1) & 3)), the
+// layout the tensor map's SWIZZLE_64B expects; rows and columns outside C are
+// clipped by the tensor store.
+template <typename T>
+__device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uint32_t (&r)[32],
+                                                uint8_t* stage, bool has_bias, float bcol,
+                                                float brow, int lane) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  epi_add_bias(v, has_bias, p.bias_per_row != 0, bcol, brow);
+  uint8_t* row = stage + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 w;
+    w.x = pack2<T>(v[8 * c + 0], v[8 * c + 1]);
+    w.y = pack2<T>(v[8 * c + 2], v[8 * c + 3]);
+    w.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
+    w.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) = w;
+  }
+}
+
+// Epilogue of one plain (non-SwiGLU) tile for one warp: TMEM columns
+// [0, BN) of its 32 lanes, loaded 32 columns at a time with the next chunk's
+// load in flight while the current one is converted, then stored through
+// the tensor-store staging (c_tma) or directly.  The chunk loop is unrolled
+// so each chunk's prefetched bias sits in a register.
+template <typename T, int BN>
+__device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMap* tmC,
+                                         uint32_t tbase, T* crow, int m, int rows, int nbase,
+                                         const T* bias_b, const EpiBias<T, BN / 32>& eb,
+                                         uint8_t* epi_stage, int q, int lane, int& epi_k,
+                                         int b1, int b2) {
+  const int mrow0 = m - lane;  // first output row of this warp
+  auto emit = [&](const uint32_t(&rr)[32], int c) {
+    const int n0 = nbase + 32 * c;
+    if (p.c_tma) {
+      uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
+      if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+      }
+      epi_chunk_stage<T>(p, rr, buf, eb.has, eb.col[c], eb.row, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (n0 < p.n && mrow0 < p.m) tma_store_4d(tmC, buf, n0, mrow0, b2, b1);
+        bulk_commit();
+      }
+      ++epi_k;
+    } else {
+      epi_chunk<T>(p, rr, crow, m, rows, n0, bias_b, eb.has, eb.col[c], eb.row);
+    }
+  };
+  if constexpr (BN == 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase, r);
+    tmem_ld_wait_tied(r);
+    emit(r, 0);
+  } else {
+    uint32_t ra[32], rb[32];
+    tmem_ld_32x32b_x32(tbase, ra);
+    tmem_ld_wait_tied(ra);
+#pragma unroll
+    for (int c = 0; c < BN / 32; c += 2) {
+      tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 1)), rb);
+      emit(ra, c);
+      tmem_ld_wait_tied(rb);
+      if (c + 2 < BN / 32) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 2)), ra);
+      emit(rb, c + 1);
+      tmem_ld_wait_tied(ra);
+    }
+  }
+}
+
+// Bytes of A a CTA loads for a tile: the full 128-row slab, only the valid
+// rows of a partial slab (tail box), or nothing past the end of M.  Rows of
+// the smem slab that are not loaded hold stale data; they only feed output
+// rows >= M, which are never stored (each output row depends on its own A
+// row only), so this changes no stored bit.
+__device__ __forceinline__ uint32_t a_slab_bytes(int valid_rows, int tail_rows) {
+  if (valid_rows >= 128) return 128u * kBK * 2;
+  if (valid_rows <= 0) return 0u;
+  return static_cast<uint32_t>(tail_rows) * kBK * 2;
+}
+
+// Shared memory of the single-CTA kernel: a data region sized for STAGES full
+// stages (A 128x64 + B BNx64), then barriers for up to kMaxStages1 stages.  At
+// run time the ring may use a denser A stride (M <= 128: only the tail rows
+// are loaded) and correspondingly more stages in the same region.
+constexpr int kMaxStages1 = 48;
+
+template <int BN, int STAGES>
+struct TcSmem {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kData = STAGES * kStageBytes;
+  static constexpr uint32_t kBarBytes = (2 * kMaxStages1 + 5) * 8 + 16;
+  static constexpr uint32_t kEpiOff = (kData + kBarBytes + kSegBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kTotal = 1024 + kEpiOff + kEpiBytes;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA_tail,
+                   const __grid_constant__ CUtensorMap tmA5,
+                   const __grid_constant__ CUtensorMap tmB5,
+                   const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
+  using L = TcSmem<BN, STAGES>;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc = idesc_f16(TypeFmt<T>::umma, kBM, BN, A_MN, B_MN);
+  constexpr uint32_t kBoxBytesMN = 64 * kBK * 2;  // one 64(N) x 64(K) box
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int nstages = p.stages;
+  const int kc = p.kchunk;            // slots per group (one tensor copy each)
+  const int ngroups = nstages / kc;
+  const int k_groups = p.k_blocks / kc;
+  const uint32_t a_stride = static_cast<uint32_t>(p.a_stride);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + nstages * a_stride;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kData);
+  uint64_t* empty_bar = full_bar + kMaxStages1;
+  uint64_t* tfull_bar = empty_bar + kMaxStages1;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* mma_done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* seg_off = reinterpret_cast<int*>(smem + L::kData + L::kBarBytes);
+  int* seg_tiles = seg_off + kMaxSegs + 1;
+  uint8_t* epi_stage = smem + L::kEpiOff;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ngroups; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 4);
+    }
+    mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    if (kc > 1) {
+      tma_prefetch_desc(&tmA5);
+      tma_prefetch_desc(&tmB5);
+    } else {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (p.seg != nullptr && warp == 2) seg_table_build(p, kBM, seg_off, seg_tiles, lane);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int64_t total = tile_total(p, seg_tiles);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        TileSeg sg;
+        const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
+        const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
+        const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
+        const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int valid = seg_valid(p, sg.rows - ti.mb * kBM);
+        const int arow = sg.base + ti.mb * kBM;
+        const uint32_t a_bytes = A_MN ? L::kABytes : a_slab_bytes(valid, p.a_tail_rows);
+        for (int kb = 0; kb < k_groups; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * kc * a_stride;
+          uint8_t* b_dst = sB + stage * kc * L::kBBytes;
+          mbar_arrive_expect_tx(&full_bar[stage],
+                                static_cast<uint32_t>(kc) * (a_bytes + L::kBBytes));
+          if (kc > 1) {
+            // kc consecutive k-blocks of A and B, one copy each; the smem
+            // image equals kc consecutive single-block slots
+            tma_load_5d(a_dst, &tmA5, &full_bar[stage], 0, arow, kb * kc, a2, a1);
+            tma_load_5d(b_dst, &tmB5, &full_bar[stage], 0, ti.nb * BN, kb * kc, b2, b1);
+          } else if constexpr (!A_MN) {
+            if (valid >= kBM)
+              tma_load_4d(a_dst, &tmA, &full_bar[stage], kb * kBK, arow, a2, a1);
+            else
+              tma_load_4d(a_dst, &tmA_tail, &full_bar[stage], kb * kBK, arow, a2, a1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) {
+              tma_load_4d(a_dst + j * kBoxBytesMN, &tmA, &full_bar[stage], arow + j * 64,
+                          kb * kBK, a2, a1);
+            }
+          }
+          if (kc == 1) {
+            if constexpr (!B_MN) {
+              tma_load_4d(b_dst, &tmB, &full_bar[stage], kb * kBK, ti.nb * BN, b2, b1);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) {
+                tma_load_4d(b_dst + j * kBoxBytesMN, &tmB, &full_bar[stage],
+                            ti.nb * BN + j * 64, kb * kBK, b2, b1);
+              }
+            }
+          }
+          ++issued;
+          if (++stage == ngroups) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the last min(issued, ngroups) loads must land before the CTA
+      // releases its shared memory (normally they already have).
+      const int64_t pending = issued < ngroups ? issued : ngroups;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int64_t i = 0; i < pending; ++i) {
+        if (--s < 0) {
+          s = ngroups - 1;
+          ph ^= 1u;
+        }
+        if (!mbar_wait_drain(&full_bar[s], ph)) raise_status(p.status, BIO_DEV_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_groups; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int c = 0; c < kc; ++c) {
+            const int slot = stage * kc + c;
+            const uint32_t a_addr = smem_u32(sA + slot * a_stride);
+            const uint32_t b_addr = smem_u32(sB + slot * L::kBBytes);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t adesc = A_MN ? smem_desc_sw128(a_addr + kk * 2048, kBoxBytesMN, 1024)
+                                          : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+              const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 2048, kBoxBytesMN, 1024)
+                                          : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+              umma_f16(d_tmem, adesc, bdesc, kIdesc, (kb | c | kk) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == ngroups) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Every MMA issued by this thread must retire before TMEM is freed.
+      umma_commit(mma_done_bar);
+      if (!mbar_wait_drain(mma_done_bar, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else {
+    // -------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int epi_k = 0;  // chunks staged by this warp (tensor-store buffer parity)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const T* bias = static_cast<const T*>(p.bias);
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+      TileSeg sg;
+      const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
+      const int m = ti.mb * kBM + q * 32 + lane;
+      const int nbase = ti.nb * BN;
+      const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+      // bias loads are issued before the wait: their latency overlaps the main loop
+      const EpiBias<T, BN / 32> eb = epi_bias_load<T, BN / 32>(p, bias_b, nbase, m, sg.rows, lane);
+      const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
+                static_cast<int64_t>(sg.base + m) * p.c_sm;
+      if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
+      const uint32_t tbase =
+          tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      epi_tile<T, BN>(p, &tmC, tbase, crow, m, sg.rows, nbase, bias_b, eb, epi_stage, q, lane,
+                      epi_k, static_cast<int>(ti.b1), static_cast<int>(ti.b2));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    // tensor stores must finish before the CTA (and its staging) goes away
+    if (p.c_tma && lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Paired (cta_group::2) tensor-core GEMM: a cluster of two CTAs on two SMs
+// computes a 256 x BN tile with M=256 tcgen05.mma issued by the leader CTA.
+// CTA r loads rows [r*128, r*128+128) of the A tile and rows
+// [r*BN/2, r*BN/2 + BN/2) of the B tile into its own shared memory (plain
+// per-CTA tensor copies); the transaction bytes of both land on the leader's
+// stage barrier.  Each CTA's TMEM holds its 128 output rows x BN fp32
+// columns; each CTA's epilogue stores its own rows.  Per SM this halves the
+// B bytes per flop against the single-CTA 128 x BN tile.
+//
+// Arithmetic per output element is the same fixed sequence as the
+// single-CTA kernel family's contract: k-block 0..K/64-1, four K=16 MMAs in
+// order; the instruction shape (M=256, N=BN) is a function of (N, K, dtype).
+// ---------------------------------------------------------------------------
+constexpr int kMaxStages2 = 32;
+
+// Shared memory of the paired kernel: a data region sized for STAGES full
+// stages (A 128x64 + B (BN/2)x64), then the barriers.  At run time the ring
+// may use a denser A stride (small M, see TcGemmParams::a_stride) and more
+// stages in the same data region.
+template <int BN, int STAGES>
+struct Tc2Smem {
+  static constexpr uint32_t kABytes = 128 * kBK * 2;
+  static constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
+  static constexpr uint32_t kData = STAGES * (kABytes + kBBytes);
+  static constexpr uint32_t kBarBytes = (2 * kMaxStages2 + 5) * 8 + 16;
+  static constexpr uint32_t kEpiOff = (kData + kBarBytes + kSegBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kTotal = 1024 + kEpiOff + kEpiBytes;
+};
+
+// Bounded spin on the global timer (used only on the abort path so that copies
+// still in flight land before the CTA releases its shared memory).
+__device__ __forceinline__ void grace_spin_ns(uint64_t ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (global_timer_ns() - t0 < ns) {
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmA_tail,
+                    const __grid_constant__ CUtensorMap tmB2,
+                    const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
+  using L = Tc2Smem<BN, STAGES>;
+  constexpr int BNH = BN / 2;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc = idesc_f16(TypeFmt<T>::umma, 256, BN, A_MN, B_MN);
+  constexpr uint32_t kBoxBytesMN = 64 * kBK * 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int nstages = p.stages;
+  const uint32_t a_stride = static_cast<uint32_t>(p.a_stride);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + nstages * a_stride;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kData);
+  uint64_t* empty_bar = full_bar + kMaxStages2;
+  uint64_t* tfull_bar = empty_bar + kMaxStages2;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* mma_done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* seg_off = reinterpret_cast<int*>(smem + L::kData + L::kBarBytes);
+  int* seg_tiles = seg_off + kMaxSegs + 1;
+  uint8_t* epi_stage = smem + L::kEpiOff;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nstages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 8);
+    }
+    mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(p.swiglu && rank == 1 ? &tmB2 : &tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(tmem_slot, kTmemCols);
+    tmem_relinquish_2sm();
+  }
+  if (p.seg != nullptr && warp == 2) seg_table_build(p, 256, seg_off, seg_tiles, lane);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int64_t total = tile_total(p, seg_tiles);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < total; t += npairs) {
+        TileSeg sg;
+        const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
+        const int a2 = p.a_bcast2 ? 0 : static_cast<int>(ti.b2 / p.a_div2);
+        const int a1 = p.a_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int b2 = p.b_bcast2 ? 0 : static_cast<int>(ti.b2 / p.b_div2);
+        const int b1 = p.b_bcast1 ? 0 : static_cast<int>(ti.b1);
+        const int a_row = sg.base + ti.mb * 256 + static_cast<int>(rank) * 128;
+        const int b_row = p.swiglu ? ti.nb * BNH : ti.nb * BN + static_cast<int>(rank) * BNH;
+        const CUtensorMap* mapB = (p.swiglu && rank == 1) ? &tmB2 : &tmB;
+        const int valid0 = sg.rows - ti.mb * 256;
+        const int my_valid = seg_valid(p, valid0 - static_cast<int>(rank) * 128);
+        // A_MN operands always move full boxes (zero-filled past M)
+        const uint32_t a0 = A_MN ? L::kABytes : a_slab_bytes(seg_valid(p, valid0), p.a_tail_rows);
+        const uint32_t a1b =
+            A_MN ? L::kABytes : a_slab_bytes(seg_valid(p, valid0 - 128), p.a_tail_rows);
+        const uint32_t tx = a0 + a1b + 2 * L::kBBytes;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * a_stride;
+          uint8_t* b_dst = sB + stage * L::kBBytes;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx);
+          const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if constexpr (!A_MN) {
+            if (my_valid >= 128)
+              tma_load_4d_2sm(a_dst, &tmA, bar, kb * kBK, a_row, a2, a1);
+            else if (my_valid > 0)
+              tma_load_4d_2sm(a_dst, &tmA_tail, bar, kb * kBK, a_row, a2, a1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              tma_load_4d_2sm(a_dst + j * kBoxBytesMN, &tmA, bar, a_row + j * 64, kb * kBK, a2, a1);
+          }
+          if constexpr (!B_MN) {
+            tma_load_4d_2sm(b_dst, mapB, bar, kb * kBK, b_row, b2, b1);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BNH / 64; ++j)
+              tma_load_4d_2sm(b_dst + j * kBoxBytesMN, mapB, bar, b_row + j * 64, kb * kBK, b2, b1);
+          }
+          if (++stage == nstages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------ MMA issuer (leader CTA only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < total; t += npairs) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * a_stride);
+          const uint32_t b_addr = smem_u32(sB + stage * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? smem_desc_sw128(a_addr + kk * 2048, kBoxBytesMN, 1024)
+                                        : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 2048, kBoxBytesMN, 1024)
+                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_2sm(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_2sm_mc(&empty_bar[stage], 0x3);
+          if (++stage == nstages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_2sm_mc(&tfull_bar[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit_2sm(mma_done_bar);
+      if (!mbar_wait_drain(mma_done_bar, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
+    }
+  } else {
+    // -------------------------------- epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    int epi_k = 0;  // chunks staged by this warp (tensor-store buffer parity)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const T* bias = static_cast<const T*>(p.bias);
+    for (int64_t t = pair; t < total; t += npairs) {
+      TileSeg sg;
+      const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
+      const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+      // bias loads are issued before the wait: their latency overlaps the main loop
+      const EpiBias<T, BN / 32> eb =
+          p.swiglu ? EpiBias<T, BN / 32>{} : epi_bias_load<T, BN / 32>(p, bias_b, ti.nb * BN, m,
+                                                                    sg.rows, lane);
+      const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+
+      T* crow = static_cast<T*>(p.c) + ti.b1 * p.c_s1 + ti.b2 * p.c_s2 +
+                static_cast<int64_t>(sg.base + m) * p.c_sm;
+      if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
+      if (p.swiglu) {
+        // gate in accumulator columns [0, BNH), up in [BNH, BN); the
+        // roundings of separate gate / up GEMMs followed by bio_silu_mul
+#pragma unroll 1
+        for (int c0 = 0; c0 < BNH; c0 += 32) {
+          uint32_t rg[32], ru[32];
+          const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+          tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) + lanes, rg);
+          tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + BNH + c0) + lanes, ru);
+          tmem_ld_wait();
+          const int n0 = ti.nb * BNH + c0;
+          if (m < sg.rows && n0 < p.n) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float g = round_to<T>(__uint_as_float(rg[j]) * p.alpha);
+              const float u = round_to<T>(__uint_as_float(ru[j]) * p.alpha);
+              v[j] = round_to<T>(g / (1.f + expf(-g))) * u;
+            }
+            if (p.c_vec_ok && n0 + 32 <= p.n) {
+              uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 w;
+                w.x = pack2<T>(v[8 * j + 0], v[8 * j + 1]);
+                w.y = pack2<T>(v[8 * j + 2], v[8 * j + 3]);
+                w.z = pack2<T>(v[8 * j + 4], v[8 * j + 5]);
+                w.w = pack2<T>(v[8 * j + 6], v[8 * j + 7]);
+                dst[j] = w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.n) crow[static_cast<int64_t>(n0 + j) * p.c_sn] = from_f32<T>(v[j]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
+      }
+      {
+        const uint32_t tbase =
+            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+        epi_tile<T, BN>(p, &tmC, tbase, crow, m, sg.rows, ti.nb * BN, bias_b, eb, epi_stage, q,
+                        lane, epi_k, static_cast<int>(ti.b1), static_cast<int>(ti.b2));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    // tensor stores must finish before the CTA (and its staging) goes away
+    if (p.c_tma && lane == 0) bulk_wait_all();
+  }
+
+  // Abort path: give loads already issued (which count on the leader's
+  // barriers) a bounded time to land before shared memory is released.
+  if (threadIdx.x == 0 && *abort_flag) grace_spin_ns(200000);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace bio
+
+// ===========================================================================
+// Host side of the tensor-core path
+// ===========================================================================
+namespace bio_gemm_tc {
+
+using bio::kBK;
+using bio::kBM;
+
+// Operand view for a 4-D tensor map {inner, outer, level2, level1}.
+struct MapDims {
+  uint64_t d[4];
+  uint64_t stride_bytes[3];
+};
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Build the {inner, outer, n2, n1} view of one operand.  Returns false when the
+// strides cannot be expressed to TMA (not multiples of 16 bytes).
+inline bool operand_dims(uint64_t inner, uint64_t outer, int64_t outer_stride, int64_t batch1,
+                  int64_t s1, int64_t n2_logical, int64_t s2, int64_t div2, MapDims* out,
+                  int* bcast1, int* bcast2) {
+  const int64_t es = 2;
+  if (outer_stride <= 0 || (outer_stride * es) % 16 != 0) return false;
+  out->d[0] = inner;
+  out->d[1] = outer;
+  out->stride_bytes[0] = static_cast<uint64_t>(outer_stride * es);
+  uint64_t prev = out->stride_bytes[0] * outer;
+  prev = (prev + 15) / 16 * 16;
+  // level 2
+  const int64_t n2 = (n2_logical + div2 - 1) / div2;
+  if (s2 == 0 || n2 <= 1) {
+    *bcast2 = (s2 == 0) ? 1 : 0;
+    out->d[2] = 1;
+    out->stride_bytes[1] = prev;
+  } else {
+    if ((s2 * es) % 16 != 0 || s2 < 0) return false;
+    *bcast2 = 0;
+    out->d[2] = static_cast<uint64_t>(n2);
+    out->stride_bytes[1] = static_cast<uint64_t>(s2 * es);
+  }
+  uint64_t prev2 = out->stride_bytes[1] * out->d[2];
+  prev2 = (prev2 + 15) / 16 * 16;
+  if (s1 == 0 || batch1 <= 1) {
+    *bcast1 = (s1 == 0) ? 1 : 0;
+    out->d[3] = 1;
+    out->stride_bytes[2] = prev2;
+  } else {
+    if ((s1 * es) % 16 != 0 || s1 < 0) return false;
+    *bcast1 = 0;
+    out->d[3] = static_cast<uint64_t>(batch1);
+    out->stride_bytes[2] = static_cast<uint64_t>(s1 * es);
+  }
+  for (int i = 0; i < 3; ++i)
+    if (out->stride_bytes[i] >= (1ull << 40)) return false;
+  return true;
+}
+
+inline int encode_map(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md, uint32_t box0,
+               uint32_t box1) {
+  bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
+  if (enc == nullptr) return BIO_ERR_DRIVER;
+  const CUtensorMapDataType dt =
+      dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[4] = {md.d[0], md.d[1], md.d[2], md.d[3]};
+  cuuint64_t strides[3] = {md.stride_bytes[0], md.stride_bytes[1], md.stride_bytes[2]};
+  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
+}
+
+// Output map {n, m, batch2, batch1} of a row-contiguous 16-bit C, box
+// {32, 32, 1, 1}, 64-byte swizzle (the epilogue's staging layout).
+inline int encode_cmap(CUtensorMap* map, const bio_gemm_args* a) {
+  bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
+  if (enc == nullptr) return BIO_ERR_DRIVER;
+  const CUtensorMapDataType dt =
+      a->dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t row = static_cast<uint64_t>(a->c_sm) * 2;
+  // a batch dimension of extent 1 gets a nominal (valid) stride
+  const uint64_t s2 = a->batch2 > 1 ? static_cast<uint64_t>(a->c_s2) * 2
+                                    : row * static_cast<uint64_t>(a->m);
+  const uint64_t s1 = a->batch1 > 1 ? static_cast<uint64_t>(a->c_s1) * 2
+                                    : s2 * static_cast<uint64_t>(a->batch2);
+  if (row % 16 != 0 || s2 % 16 != 0 || s1 % 16 != 0 || row == 0 || s2 == 0 || s1 == 0)
+    return BIO_ERR_ALIGN;
+  if (row >= (1ull << 40) || s2 >= (1ull << 40) || s1 >= (1ull << 40)) return BIO_ERR_ALIGN;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a->n), static_cast<cuuint64_t>(a->m),
+                        static_cast<cuuint64_t>(a->batch2), static_cast<cuuint64_t>(a->batch1)};
+  cuuint64_t strides[3] = {row, s2, s1};
+  cuuint32_t box[4] = {32, 32, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, a->c, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
+}
+
+// K-chunked 5-D view {64, rows, K/64, n2, n1} of a K-contiguous operand (K a
+// multiple of 64): one box {64, box_rows, chunks} lands in shared memory as
+// `chunks` consecutive [box_rows][128 B] swizzled k-block images.
+inline int encode_map5(CUtensorMap* map, int dtype, const void* ptr, const MapDims& md,
+                uint32_t box_rows, uint32_t chunks) {
+  bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
+  if (enc == nullptr) return BIO_ERR_DRIVER;
+  if (md.d[0] % 64 != 0) return BIO_ERR_SHAPE;
+  const CUtensorMapDataType dt =
+      dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[5] = {64, md.d[1], md.d[0] / 64, md.d[2], md.d[3]};
+  cuuint64_t strides[4] = {md.stride_bytes[0], 128, md.stride_bytes[1], md.stride_bytes[2]};
+  cuuint32_t box[5] = {64, box_rows, chunks, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, dt, 5, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BIO_OK : BIO_ERR_ALIGN;
+}
+
+// Output tile of one call.  Every tile runs the same per-element arithmetic
+// (64-wide K blocks in increasing order, four K=16 MMAs per block into an fp32
+// TMEM accumulator, one rounding in the epilogue), so the choice below only
+// moves work between SMs and never changes a stored bit -- this is what lets
+// it depend on M (the tests run every tile on the same inputs and require
+// identical bits).
+//   m <= 128   one m-block: single-CTA 128 x BN tiles streaming B, BN the
+//              widest of 128/64/32 that still spreads over half the SMs
+//   otherwise  CTA pair, 256 x 256 (1/128 byte of operands per flop and SM),
+//              or single-CTA 128 x 128 when the pair grid would cover less
+//              than a quarter of the SMs, or single-CTA 128 x 256 when that
+//              tiling needs fewer waves over the SMs
+struct TileChoice {
+  bool pair;
+  int bn;
+};
+
+inline TileChoice pick_tile(int64_t m, int64_t n, int64_t batch, int sms) {
+  if (m <= 128) {
+    for (int bn = 128; bn >= 64; bn >>= 1)
+      if (batch * ((n + bn - 1) / bn) * 2 >= sms) return {false, bn};
+    return {false, 32};
+  }
+  if (n <= 64) return {false, 64};
+  const int64_t pair_tiles = batch * ((m + 255) / 256) * ((n + 255) / 256);
+  if (pair_tiles * 4 < sms) return {false, 128};
+  // Wave count: a wave of single-CTA 128 x 256 tiles does the work of a wave
+  // of pair tiles at ~1.11x the time (measured), so the single-CTA tiling
+  // wins only when it needs fewer waves -- M an odd multiple of 128 leaves
+  // the last pair tile of every column half empty (e.g. a 1152-channel
+  // convolution: 3 pair waves against 2 single-CTA waves).
+  const int64_t pairs = sms / 2 > 0 ? sms / 2 : 1;
+  const int64_t one_tiles = batch * ((m + 127) / 128) * ((n + 255) / 256);
+  const int64_t waves_pair = (pair_tiles + pairs - 1) / pairs;
+  const int64_t waves_one = (one_tiles + sms - 1) / sms;
+  if (waves_one * 10 < waves_pair * 9) return {false, 256};
+  return {true, 256};
+}
+
+// The tile bio_gemm runs: pick_tile, widened to one 64-column swizzle atom
+// for an N-contiguous B on the single-CTA path.
+inline TileChoice run_tile(int64_t m, int64_t n, int64_t batch, int sms, bool b_mn) {
+  TileChoice tc = pick_tile(m, n, batch, sms);
+  if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
+  return tc;
+}
+
+// Configuration reported for (n, k, dtype): the large-M tile and the K block
+// that fixes the accumulation order.
+inline TileChoice reported_tile(int64_t n) {
+  if (n <= 64) return {false, 64};
+  return {true, 256};
+}
+
+template <bool PAIR, int BN>
+constexpr int stages_for() {
+  if (PAIR) return BN == 128 ? 8 : 6;
+  return BN <= 64 ? 8 : (BN == 128 ? 6 : 4);
+}
+
+inline std::mutex g_attr_mu;
+
+template <bool PAIR, int BN, int STAGES>
+constexpr uint32_t smem_bytes() {
+  return PAIR ? bio::Tc2Smem<BN, STAGES>::kTotal : bio::TcSmem<BN, STAGES>::kTotal;
+}
+
+// Rows of A a group of the raster may hold so that the group's A panel
+// (group * BM * K * 2 bytes) stays within ~48 MB of L2.
+inline int group_rows(int64_t k, int bm, int tiles_m) {
+  const int64_t panel = static_cast<int64_t>(bm) * k * 2;
+  int64_t g = panel > 0 ? (48ll << 20) / panel : tiles_m;
+  if (g < 1) g = 1;
+  if (g > tiles_m) g = tiles_m;
+  return static_cast<int>(g);
+}
+
+// Host description of the transposed-convolution scatter epilogue.
+struct ScatterSpec {
+  int s1, s2, k0, k1, k2, o2;
+  int64_t so, o1o2;
+  bool vec;
+};
+
+template <bool PAIR, int BN, bool A_MN, bool B_MN, typename T>
+int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
+              const void* b_up = nullptr, const ScatterSpec* sc = nullptr) {
+  constexpr int STAGES = stages_for<PAIR, BN>();
+  constexpr uint32_t kSmem = smem_bytes<PAIR, BN, STAGES>();
+  constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
+  constexpr int kBoxARows = PAIR ? 128 : kBM;     // A rows each CTA loads
+  constexpr int kBoxBRows = PAIR ? BN / 2 : BN;   // B rows each CTA loads
+  auto kern = [] {
+    if constexpr (PAIR)
+      return bio::gemm_tc2_kernel<BN, STAGES, A_MN, B_MN, T>;
+    else
+      return bio::gemm_tc_kernel<BN, STAGES, A_MN, B_MN, T>;
+  }();
+
+  static bool attr_done[bio_host::kMaxDevices] = {false};
+  static int max_units[bio_host::kMaxDevices] = {0};
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (!attr_done[a->device]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
+          cudaSuccess)
+        return BIO_ERR_LAUNCH;
+      int units = bio_host::sm_count(a->device);
+      if (PAIR) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * 74, 1, 1);
+        cfg.blockDim = dim3(bio::kGemmThreads, 1, 1);
+        cfg.dynamicSmemBytes = kSmem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+          clusters = units / 2;
+        units = clusters;
+      }
+      max_units[a->device] = units;
+      attr_done[a->device] = true;
+    }
+  }
+
+  const int64_t batch = a->batch1 * a->batch2;
+  MapDims ma, mb;
+  int a_b1 = 0, a_b2 = 0, b_b1 = 0, b_b2 = 0;
+  if (!A_MN) {
+    if (!operand_dims(static_cast<uint64_t>(a->k), static_cast<uint64_t>(a->m), a->a_sm,
+                      a->batch1, a->a_s1, a->batch2, a->a_s2, a->a_div2, &ma, &a_b1, &a_b2))
+      return BIO_ERR_ALIGN;
+  } else {
+    if (!operand_dims(static_cast<uint64_t>(a->m), static_cast<uint64_t>(a->k), a->a_sk,
+                      a->batch1, a->a_s1, a->batch2, a->a_s2, a->a_div2, &ma, &a_b1, &a_b2))
+      return BIO_ERR_ALIGN;
+  }
+  if (!B_MN) {
+    if (!operand_dims(static_cast<uint64_t>(a->k), static_cast<uint64_t>(a->n), a->b_sn,
+                      a->batch1, a->b_s1, a->batch2, a->b_s2, a->b_div2, &mb, &b_b1, &b_b2))
+      return BIO_ERR_ALIGN;
+  } else {
+    if (!operand_dims(static_cast<uint64_t>(a->n), static_cast<uint64_t>(a->k), a->b_sk,
+                      a->batch1, a->b_s1, a->batch2, a->b_s2, a->b_div2, &mb, &b_b1, &b_b2))
+      return BIO_ERR_ALIGN;
+  }
+  CUtensorMap tmA, tmB, tmA_tail;
+  int st = A_MN ? encode_map(&tmA, a->dtype, a->a, ma, 64, kBK)
+                : encode_map(&tmA, a->dtype, a->a, ma, kBK, kBoxARows);
+  if (st != BIO_OK) return st;
+  const int tail_rows = static_cast<int>(((a->m % 128) + 7) / 8 * 8);
+  if (!A_MN && tail_rows > 0) {
+    st = encode_map(&tmA_tail, a->dtype, a->a, ma, kBK, static_cast<uint32_t>(tail_rows));
+    if (st != BIO_OK) return st;
+  } else {
+    tmA_tail = tmA;
+  }
+  st = B_MN ? encode_map(&tmB, a->dtype, a->b, mb, 64, kBK)
+            : encode_map(&tmB, a->dtype, a->b, mb, kBK, kBoxBRows);
+  if (st != BIO_OK) return st;
+  // SwiGLU: the up weights share the gate weights' dims and strides
+  CUtensorMap tmB2 = tmB;
+  if (b_up != nullptr) {
+    if (!PAIR || BN != 256) return BIO_ERR_ARG;
+    st = B_MN ? encode_map(&tmB2, a->dtype, b_up, mb, 64, kBK)
+              : encode_map(&tmB2, a->dtype, b_up, mb, kBK, kBoxBRows);
+    if (st != BIO_OK) return st;
+  }
+
+  bio::TcGemmParams p;
+  p.m = static_cast<int>(a->m);
+  p.n = static_cast<int>(a->n);
+  p.k = static_cast<int>(a->k);
+  p.tiles_m = static_cast<int>((a->m + kTileM - 1) / kTileM);
+  // SwiGLU tiles produce BN / 2 output columns (gate and up halves)
+  const int out_bn = b_up != nullptr ? BN / 2 : BN;
+  p.tiles_n = static_cast<int>((a->n + out_bn - 1) / out_bn);
+  p.swiglu = b_up != nullptr ? 1 : 0;
+  p.scatter = 0;
+  if (sc != nullptr) {
+    p.scatter = 1;
+    p.sc_s1 = sc->s1;
+    p.sc_s2 = sc->s2;
+    p.sc_k0 = sc->k0;
+    p.sc_k1 = sc->k1;
+    p.sc_k2 = sc->k2;
+    p.sc_kvol = sc->k0 * sc->k1 * sc->k2;
+    p.sc_o2 = sc->o2;
+    p.sc_vec = sc->vec ? 1 : 0;
+    p.sc_so = sc->so;
+    p.sc_o1o2 = sc->o1o2;
+  }
+  p.k_blocks = static_cast<int>((a->k + kBK - 1) / kBK);
+  p.group_m = group_rows(a->k, kTileM, p.tiles_m);
+  p.a_tail_rows = tail_rows;
+  p.stages = STAGES;
+  p.a_stride = 128 * kBK * 2;
+  if constexpr (PAIR) {
+    // M <= 128: no CTA ever holds a full 128-row slab, so the A stages can be
+    // packed at the tail-box stride and the freed space buys more stages.
+    if (!A_MN && a->m <= 128 && seg == nullptr) {
+      using L2 = bio::Tc2Smem<BN, STAGES>;
+      const int stride = tail_rows > 0 ? tail_rows * kBK * 2 : 128 * kBK * 2;
+      int st_n = static_cast<int>(L2::kData / static_cast<uint32_t>(stride + L2::kBBytes));
+      // the last A stage is read as a full 16 KB slab: keep it inside the region
+      while (st_n > 2 && static_cast<uint32_t>((st_n - 1) * stride + 128 * kBK * 2) >
+                             static_cast<uint32_t>(st_n * (stride + L2::kBBytes)))
+        --st_n;
+      if (st_n > bio::kMaxStages2) st_n = bio::kMaxStages2;
+      p.stages = st_n;
+      p.a_stride = stride;
+    }
+  } else {
+    // Single CTA, M <= 128: one m-block whose A slab is packed at the
+    // tail-box stride; the freed space holds more B stages.
+    if (!A_MN && a->m <= 128 && tail_rows > 0 && seg == nullptr) {
+      using L1 = bio::TcSmem<BN, STAGES>;
+      const int stride = tail_rows * kBK * 2;
+      int st_n = static_cast<int>(L1::kData / static_cast<uint32_t>(stride + L1::kBBytes));
+      // the MMA reads each A stage as a full 16 KB slab: keep the last one
+      // inside the data region
+      while (st_n > 2 && static_cast<uint32_t>((st_n - 1) * stride + 128 * kBK * 2) >
+                             static_cast<uint32_t>(st_n * (stride + L1::kBBytes)))
+        --st_n;
+      if (st_n > bio::kMaxStages1) st_n = bio::kMaxStages1;
+      p.stages = st_n;
+      p.a_stride = stride;
+    }
+  }
+  // Single CTA, one m-block, K-contiguous operands, K a multiple of 64: move
+  // kchunk k-blocks per tensor copy (fewer, larger copies in flight per SM),
+  // keeping at least three copy groups in the ring.
+  p.kchunk = 1;
+  CUtensorMap tmA5 = tmA, tmB5 = tmB;
+  if constexpr (!PAIR && !A_MN && !B_MN) {
+    if (a->m <= 128 && a->k % 64 == 0 && seg == nullptr) {
+      using L1 = bio::TcSmem<BN, STAGES>;
+      const int target = static_cast<int>((32u * 1024u) / L1::kBBytes);  // ~32 KB of B per copy
+      for (int c = 8; c >= 2; c >>= 1) {
+        if (c > target || p.k_blocks % c != 0 || p.stages / c < 3) continue;
+        const uint32_t a_rows = tail_rows > 0 ? static_cast<uint32_t>(tail_rows) : 128u;
+        if (encode_map5(&tmA5, a->dtype, a->a, ma, a_rows, static_cast<uint32_t>(c)) != BIO_OK ||
+            encode_map5(&tmB5, a->dtype, a->b, mb, static_cast<uint32_t>(BN),
+                        static_cast<uint32_t>(c)) != BIO_OK) {
+          tmA5 = tmA;
+          tmB5 = tmB;
+          break;
+        }
+        p.kchunk = c;
+        p.stages = p.stages / c * c;
+        break;
+      }
+    }
+  }
+  p.batch2 = a->batch2;
+  p.total_tiles = batch * p.tiles_m * p.tiles_n;
+  p.seg = seg;
+  p.nseg = static_cast<int>(a->batch1);
+  if (seg != nullptr) {
+    // upper bound: a segment of r rows has at most r / kTileM + 1 m-tiles
+    p.total_tiles = (a->m / kTileM + a->batch1) * p.tiles_n;
+    p.group_m = group_rows(a->k, kTileM, static_cast<int>(a->m / kTileM + a->batch1));
+  }
+  p.a_div2 = static_cast<int>(a->a_div2);
+  p.b_div2 = static_cast<int>(a->b_div2);
+  p.a_bcast1 = a_b1;
+  p.a_bcast2 = a_b2;
+  p.b_bcast1 = b_b1;
+  p.b_bcast2 = b_b2;
+  p.c = a->c;
+  p.c_sm = a->c_sm;
+  p.c_sn = a->c_sn;
+  p.c_s1 = a->c_s1;
+  p.c_s2 = a->c_s2;
+  p.bias = a->bias;
+  p.bias_s2 = a->bias_s2;
+  p.bias_per_row = (a->flags & BIO_GEMM_BIAS_PER_ROW) ? 1 : 0;
+  p.alpha = a->alpha;
+  p.c_vec_ok = (a->c_sn == 1 && aligned16(a->c) && (a->c_sm * 2) % 16 == 0 &&
+                (a->c_s1 * 2) % 16 == 0 && (a->c_s2 * 2) % 16 == 0)
+                   ? 1
+                   : 0;
+  p.status = bio_host::status_word(a->device);
+  // Plain mode writes C through tensor stores when C has a tensor map
+  // (row-contiguous, 16-byte aligned rows and batches, at least one 32 x 32
+  // box); otherwise (and in the segmented, SwiGLU and scatter modes, whose
+  // rows or layout a box cannot express) the epilogue stores directly.
+  CUtensorMap tmC = tmA;
+  p.c_tma = 0;
+  if (seg == nullptr && b_up == nullptr && sc == nullptr && p.c_vec_ok && a->m >= 32 &&
+      a->n >= 32 && encode_cmap(&tmC, a) == BIO_OK)
+    p.c_tma = 1;
+
+  const int64_t units = max_units[a->device];
+  if (units <= 0) return BIO_ERR_LAUNCH;
+  const int64_t n_units = p.total_tiles < units ? p.total_tiles : units;
+  const int64_t grid = PAIR ? 2 * n_units : n_units;
+  if constexpr (PAIR)
+    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
+                                                                          tmB2, tmC, p);
+  else
+    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
+                                                                          tmA5, tmB5, tmC, p);
+  return bio_host::launch_status(cudaGetLastError());
+}
+
+// Tile configurations compiled into the library: (pair, bn).
+inline bool tile_supported(const TileChoice& tc) {
+  if (tc.pair) return tc.bn == 128 || tc.bn == 256;
+  return tc.bn == 32 || tc.bn == 64 || tc.bn == 128 || tc.bn == 256;
+}
+
+// One operand layout and dtype: launches the tile `tc` (b_up: SwiGLU mode,
+// CTA pair 256 only).  Each (A_MN, B_MN, T) is instantiated in its own
+// translation unit (bio_gemm_tc_*.cu) so the kernels compile in parallel.
+template <bool A_MN, bool B_MN, typename T>
+int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, const int* seg,
+                cudaStream_t stream, const ScatterSpec* sc, const void* b_up) {
+  if (tc.pair) {
+    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    return launch_tc<true, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+  }
+  switch (tc.bn) {
+    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+  }
+}
+
+#define BIO_GEMM_TC_DECL(KW, A_MN, B_MN, T)                                                   \
+  KW template int dispatch_bn<A_MN, B_MN, T>(const bio_gemm_args*, const TileChoice&,       \
+                                             const int*, cudaStream_t, const ScatterSpec*, \
+                                             const void*);
+BIO_GEMM_TC_DECL(extern, false, false, __nv_bfloat16)
+BIO_GEMM_TC_DECL(extern, false, true, __nv_bfloat16)
+BIO_GEMM_TC_DECL(extern, true, false, __nv_bfloat16)
+BIO_GEMM_TC_DECL(extern, true, true, __nv_bfloat16)
+BIO_GEMM_TC_DECL(extern, false, false, __half)
+BIO_GEMM_TC_DECL(extern, false, true, __half)
+BIO_GEMM_TC_DECL(extern, true, false, __half)
+BIO_GEMM_TC_DECL(extern, true, true, __half)
+
+template <typename T>
+int dispatch_tc(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream, bool a_mn,
+                bool b_mn, const int* seg = nullptr, const ScatterSpec* sc = nullptr,
+                const void* b_up = nullptr) {
+  if (a_mn) {
+    return b_mn ? dispatch_bn<true, true, T>(a, tc, seg, stream, sc, b_up)
+                : dispatch_bn<true, false, T>(a, tc, seg, stream, sc, b_up);
+  }
+  return b_mn ? dispatch_bn<false, true, T>(a, tc, seg, stream, sc, b_up)
+              : dispatch_bn<false, false, T>(a, tc, seg, stream, sc, b_up);
+}
+
+}  // namespace bio_gemm_tc

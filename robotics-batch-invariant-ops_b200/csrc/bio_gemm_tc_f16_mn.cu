@@ -1,0 +1,8 @@
+// Tensor-core GEMM kernels for __half, A M-contiguous, B N-contiguous:
+// one of the eight instantiation units of bio_gemm_tc.cuh (split so that the
+// kernels compile in parallel).
+#include "bio_gemm_tc.cuh"
+
+namespace bio_gemm_tc {
+BIO_GEMM_TC_DECL(, true, true, __half)
+}  // namespace bio_gemm_tc
