@@ -97,6 +97,7 @@ BIO_API int bio_clear_device_status(int device);
  * (batch_invariant_ops.py:61-139, 271-343) and bmm_kernel_persistent /
  * bmm_persistent (batch_invariant_ops.py:143-229, 346-431). */
 #define BIO_GEMM_BIAS_PER_ROW 1 /* flags: bias indexed by m instead of n */
+#define BIO_GEMM_GATE_GELU_TANH 2 /* flags (bio_gemm_swiglu only): GELU-tanh gate */
 
 typedef struct bio_gemm_args {
   int32_t dtype;   /* BIO_F32 / BIO_F16 / BIO_BF16: A, B, C and bias dtype */
@@ -180,8 +181,11 @@ BIO_API int bio_gemm_segmented(const bio_gemm_args* args, const int32_t* seg, vo
 /* Fused SwiGLU expert GEMM (f16/bf16): C = silu(A·gateᵀ) * (A·upᵀ) with the
  * roundings of two bio_gemm calls followed by bio_silu_mul (gate and up
  * rounded to the dtype, silu rounded, product rounded), bit for bit.  `args`
- * describes the gate GEMM (b = gate weights, n = output columns, no bias, no
- * flags); `up` has the same dims and strides as b.  One CTA pair computes a
+ * describes the gate GEMM (b = gate weights, n = output columns, no bias;
+ * flags 0, or BIO_GEMM_GATE_GELU_TANH for GeGLU: the gate activation is
+ * 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))) in fp32, the rounding steps
+ * of F.gelu(gate, approximate="tanh") * up); `up` has the same dims and
+ * strides as b.  One CTA pair computes a
  * 256-row tile of gate and up for 128 output columns in one 256-wide
  * accumulator (the leader loads gate rows, its peer the same up rows), so A
  * is read once and the gate/up outputs never reach HBM.  `seg` (optional)

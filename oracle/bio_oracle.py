@@ -298,6 +298,20 @@ def rms_norm(x, normalized_ndim: int, weight=None, eps=None):
     return out
 
 
+def gated_linear(x, weight, activation="gelu_tanh"):
+    """act(x W_g^T) * (x W_u^T) with weight [2F, K] = [W_g; W_u] (a transformer
+    MLP's gated input projection; act = GELU in its tanh form, or silu).  No
+    counterpart in the reference, which leaves MLP activations to stock torch."""
+    y = linear(x, weight)
+    f = y.shape[-1] // 2
+    g, u = y[..., :f], y[..., f:]
+    if activation == "gelu_tanh":
+        act = 0.5 * g * (1.0 + torch.tanh(math.sqrt(2.0 / math.pi) * (g + 0.044715 * g ** 3)))
+    else:
+        act = g / (1.0 + torch.exp(-g))
+    return act * u
+
+
 # ---------------------------------------------------------------------------
 # Mixture of experts
 # ---------------------------------------------------------------------------

@@ -15,6 +15,7 @@ from .batch_invariant_ops import (
     conv_transpose3d_batch_invariant,
     disable_batch_invariant_mode,
     enable_batch_invariant_mode,
+    gated_linear_batch_invariant,
     get_batch_invariant_attention_block_size,
     is_batch_invariant_mode_enabled,
     layer_norm_batch_invariant,
@@ -55,7 +56,9 @@ __all__ = [
     "get_batch_invariant_attention_block_size",
     "AttentionBlockSize",
     "deterministic_token_choice_moe",
-    # additions (no counterpart in the reference): fused normalisations
+    # additions (no counterpart in the reference): fused normalisations and
+    # the fused gated MLP input projection
     "layer_norm_batch_invariant",
     "rms_norm_batch_invariant",
+    "gated_linear_batch_invariant",
 ]

@@ -111,7 +111,10 @@ def sdpa(q, k, v, attn_mask, is_causal, scale):
     v4 = _dim_contiguous(v.reshape(nb, hkv, lk, dv))
     if q.dtype != torch.float32:
         q4, k4, v4 = _tma_ready(q4), _tma_ready(k4), _tma_ready(v4)
-    out = torch.empty((nb, h, lq, dv), device=q.device, dtype=q.dtype)
+    # Stored token-major ([nb, Lq, H, Dv] memory, returned as the [nb, H, Lq, Dv]
+    # view), as flash attention lays out its output, so that the usual
+    # out.transpose(-3, -2).reshape(..., H * Dv) that follows is a view.
+    out = torch.empty((nb, lq, h, dv), device=q.device, dtype=q.dtype).transpose(1, 2)
     if out.numel() == 0:
         return out.reshape(*lead, h, lq, dv)
     a = _AttnArgs()

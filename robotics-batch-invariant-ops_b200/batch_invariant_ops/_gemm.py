@@ -215,6 +215,7 @@ def _launch(
     exact_f32: bool = True,
     segments: torch.Tensor | None = None,
     swiglu_up: Operand | None = None,
+    gate_gelu: bool = False,
 ) -> None:
     """Enqueue one GEMM on the current stream of ``c``'s device.
 
@@ -222,7 +223,8 @@ def _launch(
     bio_gemm_segmented: segment s owns rows [segments[s], segments[s+1]) of A
     and C and multiplies them by B batch s.  ``swiglu_up`` (an operand with
     the same layout as ``b``) selects bio_gemm_swiglu: C = silu(A·B) * (A·up)
-    with the roundings of separate GEMMs and bio_silu_mul.
+    with the roundings of separate GEMMs and bio_silu_mul; with ``gate_gelu``
+    the gate activation is GELU-tanh instead of silu (GeGLU).
 
     fp32 runs on the int8 tensor cores with exact integer slices
     (bio_gemm_f32_exact, workspace from the caching allocator) whenever that
@@ -231,7 +233,8 @@ def _launch(
     tile_n) selects bio_gemm_tiled, an explicit output tile."""
     args = _lib.GemmArgs()
     args.dtype = _lib.DTYPE_CODE[c.dtype]
-    args.flags = _lib.BIO_GEMM_BIAS_PER_ROW if bias_per_row else 0
+    args.flags = (_lib.BIO_GEMM_BIAS_PER_ROW if bias_per_row else 0) | (
+        _lib.BIO_GEMM_GATE_GELU_TANH if gate_gelu else 0)
     args.batch1 = batch1
     args.batch2 = batch2
     args.m, args.n, args.k = m, n, k
@@ -329,6 +332,27 @@ def mm(
         tile=tile, exact_f32=exact_f32, alpha=alpha,
     )
     return c
+
+
+def gated(x: torch.Tensor, weight: torch.Tensor, gelu: bool) -> torch.Tensor | None:
+    """act(x @ weight[:F]^T) * (x @ weight[F:]^T) for x [M, K], weight [2F, K]
+    (f16/bf16) in one fused GEMM (bio_gemm_swiglu; act = GELU-tanh or silu),
+    with the rounding steps of the separate linear, activation and product.
+    None when the two weight halves do not share one layout."""
+    m, k = x.shape
+    f = weight.shape[0] // 2
+    out = torch.empty((m, f), device=x.device, dtype=x.dtype)
+    if m == 0 or f == 0:
+        return out
+    gate, up = weight[:f], weight[f:]
+    opa = operand_a(x, 1, 1, m, k, x.stride(0), x.stride(1), 0, 0)
+    opg = operand_b(gate, 1, 1, k, f, gate.stride(1), gate.stride(0), 0, 0)
+    opu = operand_b(up, 1, 1, k, f, up.stride(1), up.stride(0), 0, 0)
+    if (opg.s_row, opg.s_col) != (opu.s_row, opu.s_col):
+        return None
+    launch(opa, opg, out, batch1=1, batch2=1, m=m, n=f, k=k, c_sm=f, c_sn=1, c_s1=0, c_s2=0,
+           swiglu_up=opu, gate_gelu=gelu)
+    return out
 
 
 def bmm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tensor:

@@ -34,6 +34,7 @@ BIO_DEV_TIMEOUT = 1
 BIO_DEV_INDEX = 2
 
 BIO_GEMM_BIAS_PER_ROW = 1
+BIO_GEMM_GATE_GELU_TANH = 2
 
 BIO_NORM_LAYER = 0
 BIO_NORM_RMS = 1

@@ -133,6 +133,37 @@ def linear_batch_invariant(input, weight, bias=None):
     return output.reshape(output_shape)
 
 
+def gated_linear_batch_invariant(input, weight, activation="gelu_tanh"):
+    """Gated linear unit in one fused GEMM: with ``weight`` [2F, K] holding the
+    gate rows first, returns act(input @ weight[:F]^T) * (input @ weight[F:]^T)
+    of shape [..., F] -- the ``gate, up = F.linear(input, weight).split(F, -1)``
+    followed by ``F.gelu(gate, approximate="tanh") * up`` (activation
+    "gelu_tanh", GeGLU) or ``F.silu(gate) * up`` ("silu", SwiGLU) of a
+    transformer MLP, with the same rounding steps (gate and up rounded to the
+    dtype, the activation rounded, the product rounded).  For f16/bf16 the
+    gate and up accumulators share one tile of the tensor-core GEMM and the
+    gate/up activations never reach HBM.  Each output row depends on its own
+    input row only, so the result is batch invariant.  Not in the reference,
+    which has no fused MLP operator."""
+    _require_cuda(input, weight)
+    if activation not in ("gelu_tanh", "silu"):
+        raise ValueError(f"unsupported gated activation: {activation}")
+    assert weight.ndim == 2 and weight.shape[0] % 2 == 0, "gated weight must be [2F, K]"
+    assert input.shape[-1] == weight.shape[-1], "Incompatible dimensions"
+    assert input.dtype == weight.dtype, "input and weight dtypes must match"
+    f = weight.shape[0] // 2
+    flat = input.reshape(-1, input.shape[-1])
+    out = None
+    if input.dtype in (torch.float16, torch.bfloat16) and flat.shape[1] > 0:
+        out = _gemm.gated(flat, weight, activation == "gelu_tanh")
+    if out is None:
+        gate, up = linear_batch_invariant(flat, weight).split(f, dim=-1)
+        act = (torch.nn.functional.gelu(gate, approximate="tanh") if activation == "gelu_tanh"
+               else torch.nn.functional.silu(gate))
+        out = act * up
+    return out.reshape(*input.shape[:-1], f)
+
+
 def bmm_batch_invariant(a, b):
     return bmm_persistent(a, b)
 

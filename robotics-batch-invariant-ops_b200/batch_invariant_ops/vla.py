@@ -7,8 +7,9 @@ prefix keys/values of its layer and to the action tokens, integrated with a
 fixed number of flow-matching (Euler) steps over an action chunk.  Written
 with stock torch.nn.functional calls only, so that under
 ``set_batch_invariant_mode`` every GEMM, convolution, attention, softmax and
-mean runs on this library's kernels; the weights are random (no checkpoint)
-and the inputs synthetic.
+mean runs on this library's kernels; the GeGLU input projections call the
+library's fused gated GEMM (``gated_linear_batch_invariant``) when the mode
+is on.  The weights are random (no checkpoint) and the inputs synthetic.
 
 ``VLAConfig.full()`` is the BASELINE size (So400m-like 27 x 1152 vision
 tower, Gemma-2B-like 18 x 2048 prefix LM with 8 query / 1 KV heads of 256,
@@ -24,6 +25,8 @@ import math
 
 import torch
 import torch.nn.functional as F
+
+from .batch_invariant_ops import gated_linear_batch_invariant, is_batch_invariant_mode_enabled
 
 
 @dataclasses.dataclass(frozen=True)
@@ -164,6 +167,10 @@ class PiZeroStyleVLA(torch.nn.Module):
         return q, k, v
 
     def _geglu(self, h, w_in, w_out, width):
+        if is_batch_invariant_mode_enabled() and h.is_cuda:
+            # the library's fused GeGLU GEMM: same rounding steps as the
+            # stock composition below, without the gate/up round trip to HBM
+            return F.linear(gated_linear_batch_invariant(h, w_in, "gelu_tanh"), w_out)
         gate, up = F.linear(h, w_in).split(width, dim=-1)
         return F.linear(F.gelu(gate, approximate="tanh") * up, w_out)
 

@@ -42,6 +42,18 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
 template <typename T>
 __device__ __forceinline__ float round_to(float v) { return to_f32(from_f32<T>(v)); }
 
+// GELU, tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) in fp32,
+// evaluated in the order PyTorch's elementwise GELU kernel uses for a 16-bit
+// input (cube by two products, inner sum, scale, then the outer products),
+// so a fused epilogue and F.gelu(approximate="tanh") round alike.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  constexpr float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  constexpr float kKappa = 0.044715f;
+  const float x_cube = x * x * x;
+  const float inner = kBeta * (x + kKappa * x_cube);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
 // ---------------------------------------------------------------------------
 // Bounded waits
 // ---------------------------------------------------------------------------

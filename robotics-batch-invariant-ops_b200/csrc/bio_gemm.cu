@@ -354,7 +354,9 @@ int dispatch_swiglu(const bio_gemm_args* a, const int* seg, const void* up, cuda
 // null; seg optional).
 int grouped_impl(const bio_gemm_args* a, const int32_t* seg, const void* up, void* stream_v) {
   if (a == nullptr) return BIO_ERR_ARG;
-  if (a->flags != 0 || a->a_div2 < 1 || a->b_div2 < 1) return BIO_ERR_ARG;
+  // the only flag of the grouped modes: GELU-tanh instead of silu (gated only)
+  const int32_t allowed = up != nullptr ? BIO_GEMM_GATE_GELU_TANH : 0;
+  if ((a->flags & ~allowed) != 0 || a->a_div2 < 1 || a->b_div2 < 1) return BIO_ERR_ARG;
   if (up != nullptr && a->bias != nullptr) return BIO_ERR_ARG;
   if (a->dtype != BIO_F16 && a->dtype != BIO_BF16) return BIO_ERR_DTYPE;
   if (a->m < 0 || a->n < 0 || a->k < 1 || a->batch1 < 1 || a->batch2 < 1) return BIO_ERR_SHAPE;

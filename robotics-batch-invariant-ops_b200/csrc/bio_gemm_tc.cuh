@@ -34,7 +34,8 @@ struct TcGemmParams {
   // SwiGLU mode (CTA pair, BN = 256): the leader CTA's half of the B tile
   // comes from tmB (gate) and the peer's from tmB2 (up) at the same rows, so
   // accumulator columns [0, 128) hold gate and [128, 256) up for 128 output
-  // columns; the epilogue stores round(silu(round(gate)) * round(up)).
+  // columns; the epilogue stores round(act(round(gate)) * round(up)) with
+  // act = silu (swiglu == 1) or the tanh form of GELU (swiglu == 2).
   int swiglu;
   // Transposed-convolution scatter (stride == kernel): tile row m is input
   // position (s0, s1, s2), column n is (o, t0, t1, t2); the element is
@@ -981,7 +982,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
       if (p.swiglu) {
         // gate in accumulator columns [0, BNH), up in [BNH, BN); the
-        // roundings of separate gate / up GEMMs followed by bio_silu_mul
+        // roundings of separate gate / up GEMMs followed by the elementwise
+        // activation and product (bio_silu_mul, or GELU-tanh then multiply)
 #pragma unroll 1
         for (int c0 = 0; c0 < BNH; c0 += 32) {
           uint32_t rg[32], ru[32];
@@ -996,7 +998,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < 32; ++j) {
               const float g = round_to<T>(__uint_as_float(rg[j]) * p.alpha);
               const float u = round_to<T>(__uint_as_float(ru[j]) * p.alpha);
-              v[j] = round_to<T>(g / (1.f + expf(-g))) * u;
+              const float act = p.swiglu == 2 ? gelu_tanh(g) : g / (1.f + expf(-g));
+              v[j] = round_to<T>(act) * u;
             }
             if (p.c_vec_ok && n0 + 32 <= p.n) {
               uint4* dst = reinterpret_cast<uint4*>(crow + n0);
@@ -1356,7 +1359,7 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
   // SwiGLU tiles produce BN / 2 output columns (gate and up halves)
   const int out_bn = b_up != nullptr ? BN / 2 : BN;
   p.tiles_n = static_cast<int>((a->n + out_bn - 1) / out_bn);
-  p.swiglu = b_up != nullptr ? 1 : 0;
+  p.swiglu = b_up == nullptr ? 0 : ((a->flags & BIO_GEMM_GATE_GELU_TANH) ? 2 : 1);
   p.scatter = 0;
   if (sc != nullptr) {
     p.scatter = 1;
