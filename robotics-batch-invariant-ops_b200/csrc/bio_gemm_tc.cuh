@@ -13,7 +13,8 @@ namespace bio {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 192;   // single-CTA kernel: 2 + 4 epilogue warps
+constexpr int kGemm2Threads = 320;  // CTA pair: 2 + 8 epilogue warps (2 per TMEM lane quarter)
 
 struct TcGemmParams {
   int m, n, k;
@@ -93,8 +94,9 @@ __device__ __forceinline__ TileIdx decode_tile(int64_t t, int tiles_m, int tiles
 // and an exclusive prefix of m-tiles per segment in shared memory.
 constexpr int kMaxSegs = 1024;
 constexpr uint32_t kSegBytes = 2 * (kMaxSegs + 1) * 4;
-// Epilogue staging for tensor stores: 4 warps x 2 buffers x (32 rows x 64 B).
-constexpr uint32_t kEpiBytes = 4 * 2 * 2048;
+// Epilogue staging for tensor stores: 16 KB = 8 buffers of 32 rows x 64 B
+// (single-CTA kernel: 4 warps x 2 buffers; CTA pair: 8 warps x 1 buffer).
+constexpr uint32_t kEpiBytes = 8 * 2048;
 
 struct TileSeg {
   int base, rows;  // first A/C row of the tile's segment and its row count
@@ -440,24 +442,24 @@ __device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uin
   }
 }
 
-// Epilogue of one plain (non-SwiGLU) tile for one warp: TMEM columns
-// [0, BN) of its 32 lanes, loaded 32 columns at a time with the next chunk's
-// load in flight while the current one is converted, then stored through
-// the tensor-store staging (c_tma) or directly.  The chunk loop is unrolled
-// so each chunk's prefetched bias sits in a register.
-template <typename T, int BN>
+// Epilogue of one plain (non-SwiGLU) tile for one warp: NCH chunks of 32
+// TMEM columns of its 32 lanes starting at tbase (output columns from
+// nbase), loaded with the next chunk's load in flight while the current one
+// is converted, then stored through the tensor-store staging (c_tma; NBUF
+// 2 KB buffers at `stage`) or directly.  The chunk loop is unrolled so each
+// chunk's prefetched bias sits in a register.
+template <typename T, int NCH, int NBUF>
 __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMap* tmC,
                                          uint32_t tbase, T* crow, int m, int rows, int nbase,
-                                         const T* bias_b, const EpiBias<T, BN / 32>& eb,
-                                         uint8_t* epi_stage, int q, int lane, int& epi_k,
-                                         int b1, int b2) {
+                                         const T* bias_b, const EpiBias<T, NCH>& eb,
+                                         uint8_t* stage, int lane, int& epi_k, int b1, int b2) {
   const int mrow0 = m - lane;  // first output row of this warp
   auto emit = [&](const uint32_t(&rr)[32], int c) {
     const int n0 = nbase + 32 * c;
     if (p.c_tma) {
-      uint8_t* buf = epi_stage + q * 4096 + (epi_k & 1) * 2048;
-      if (epi_k >= 2) {  // this buffer's store (two chunks ago) has read it
-        if (lane == 0) bulk_wait_read<1>();
+      uint8_t* buf = stage + (NBUF == 2 ? (epi_k & 1) * 2048 : 0);
+      if (epi_k >= NBUF) {  // this buffer's store (NBUF chunks ago) has read it
+        if (lane == 0) bulk_wait_read<NBUF - 1>();
         __syncwarp();
       }
       epi_chunk_stage<T>(p, rr, buf, eb.has, eb.col[c], eb.row, lane);
@@ -472,7 +474,7 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
       epi_chunk<T>(p, rr, crow, m, rows, n0, bias_b, eb.has, eb.col[c], eb.row);
     }
   };
-  if constexpr (BN == 32) {
+  if constexpr (NCH == 1) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tbase, r);
     tmem_ld_wait_tied(r);
@@ -482,11 +484,11 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
     tmem_ld_32x32b_x32(tbase, ra);
     tmem_ld_wait_tied(ra);
 #pragma unroll
-    for (int c = 0; c < BN / 32; c += 2) {
+    for (int c = 0; c < NCH; c += 2) {
       tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 1)), rb);
       emit(ra, c);
       tmem_ld_wait_tied(rb);
-      if (c + 2 < BN / 32) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 2)), ra);
+      if (c + 2 < NCH) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 2)), ra);
       emit(rb, c + 1);
       tmem_ld_wait_tied(ra);
     }
@@ -733,8 +735,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (p.scatter && m < sg.rows) crow += scatter_row_off(p, m);
       const uint32_t tbase =
           tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      epi_tile<T, BN>(p, &tmC, tbase, crow, m, sg.rows, nbase, bias_b, eb, epi_stage, q, lane,
-                      epi_k, static_cast<int>(ti.b1), static_cast<int>(ti.b2));
+      epi_tile<T, BN / 32, 2>(p, &tmC, tbase, crow, m, sg.rows, nbase, bias_b, eb,
+                              epi_stage + q * 4096, lane, epi_k, static_cast<int>(ti.b1),
+                              static_cast<int>(ti.b2));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -793,7 +796,7 @@ __device__ __forceinline__ void grace_spin_ns(uint64_t ns) {
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, typename T>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA_tail,
@@ -837,7 +840,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], 8);
+      mbar_init(&tempty_bar[i], 16);  // 8 epilogue warps in each of the two CTAs
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
@@ -958,9 +961,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait_drain(mma_done_bar, 0)) raise_status(p.status, BIO_DEV_TIMEOUT);
     }
   } else {
-    // -------------------------------- epilogue (warps 2..5, both CTAs)
+    // -------------------------------- epilogue (warps 2..9, both CTAs)
+    // Warps w and w + 4 share TMEM lane quarter q = w & 3 and split the
+    // tile's columns: half h = (w - 2) >> 2 takes columns [h BN/2, (h+1) BN/2)
+    // (SwiGLU: output columns [h BNH/2, (h+1) BNH/2)).
     const int q = warp & 3;
-    int epi_k = 0;  // chunks staged by this warp (tensor-store buffer parity)
+    const int h = (warp - 2) >> 2;
+    int epi_k = 0;  // chunks staged by this warp (tensor-store buffer reuse)
     int acc = 0;
     uint32_t acc_phase = 0;
     const T* bias = static_cast<const T*>(p.bias);
@@ -969,9 +976,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const TileIdx ti = tile_at(t, p, seg_off, seg_tiles, &sg);
       const int m = ti.mb * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
       const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
+      const int nhalf = ti.nb * BN + h * (BN / 2);  // first output column of this warp
       // bias loads are issued before the wait: their latency overlaps the main loop
-      const EpiBias<T, BN / 32> eb =
-          p.swiglu ? EpiBias<T, BN / 32>{} : epi_bias_load<T, BN / 32>(p, bias_b, ti.nb * BN, m,
+      const EpiBias<T, BN / 64> eb =
+          p.swiglu ? EpiBias<T, BN / 64>{} : epi_bias_load<T, BN / 64>(p, bias_b, nhalf, m,
                                                                     sg.rows, lane);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
@@ -985,7 +993,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         // roundings of separate gate / up GEMMs followed by the elementwise
         // activation and product (bio_silu_mul, or GELU-tanh then multiply)
 #pragma unroll 1
-        for (int c0 = 0; c0 < BNH; c0 += 32) {
+        for (int c0 = h * (BNH / 2); c0 < (h + 1) * (BNH / 2); c0 += 32) {
           uint32_t rg[32], ru[32];
           const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
           tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + c0) + lanes, rg);
@@ -994,12 +1002,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const int n0 = ti.nb * BNH + c0;
           if (m < sg.rows && n0 < p.n) {
             float v[32];
+            if (p.swiglu == 2) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float g = round_to<T>(__uint_as_float(rg[j]) * p.alpha);
-              const float u = round_to<T>(__uint_as_float(ru[j]) * p.alpha);
-              const float act = p.swiglu == 2 ? gelu_tanh(g) : g / (1.f + expf(-g));
-              v[j] = round_to<T>(act) * u;
+              for (int j = 0; j < 32; ++j) {
+                const float g = round_to<T>(__uint_as_float(rg[j]) * p.alpha);
+                const float u = round_to<T>(__uint_as_float(ru[j]) * p.alpha);
+                v[j] = round_to<T>(gelu_tanh(g)) * u;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float g = round_to<T>(__uint_as_float(rg[j]) * p.alpha);
+                const float u = round_to<T>(__uint_as_float(ru[j]) * p.alpha);
+                v[j] = round_to<T>(g / (1.f + expf(-g))) * u;
+              }
             }
             if (p.c_vec_ok && n0 + 32 <= p.n) {
               uint4* dst = reinterpret_cast<uint4*>(crow + n0);
@@ -1027,10 +1043,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         continue;
       }
       {
-        const uint32_t tbase =
-            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-        epi_tile<T, BN>(p, &tmC, tbase, crow, m, sg.rows, ti.nb * BN, bias_b, eb, epi_stage, q,
-                        lane, epi_k, static_cast<int>(ti.b1), static_cast<int>(ti.b2));
+        const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN + h * (BN / 2)) +
+                               (static_cast<uint32_t>(q * 32) << 16);
+        epi_tile<T, BN / 64, 1>(p, &tmC, tbase, crow, m, sg.rows, nhalf, bias_b, eb,
+                                epi_stage + (warp - 2) * 2048, lane, epi_k,
+                                static_cast<int>(ti.b1), static_cast<int>(ti.b2));
       }
       tc_fence_before();
       __syncwarp();
@@ -1288,7 +1305,7 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
       if (PAIR) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * 74, 1, 1);
-        cfg.blockDim = dim3(bio::kGemmThreads, 1, 1);
+        cfg.blockDim = dim3(bio::kGemm2Threads, 1, 1);
         cfg.dynamicSmemBytes = kSmem;
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -1480,8 +1497,8 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
   const int64_t n_units = p.total_tiles < units ? p.total_tiles : units;
   const int64_t grid = PAIR ? 2 * n_units : n_units;
   if constexpr (PAIR)
-    kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
-                                                                          tmB2, tmC, p);
+    kern<<<static_cast<unsigned>(grid), bio::kGemm2Threads, kSmem, stream>>>(tmA, tmB, tmA_tail,
+                                                                           tmB2, tmC, p);
   else
     kern<<<static_cast<unsigned>(grid), bio::kGemmThreads, kSmem, stream>>>(tmA, tmB, tmA_tail,
                                                                           tmA5, tmB5, tmC, p);
