@@ -51,8 +51,15 @@ def _sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
-def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
+def _headers_mtime() -> float:
+    return max(p.stat().st_mtime for p in [*CSRC.glob("*.cuh"), *INCLUDE.glob("*.h"), Path(__file__)])
+
+
+def _compile(src: Path, verbose_ptxas: bool, incremental: bool = False) -> tuple[Path, str]:
     obj = BUILD / (src.stem + ".o")
+    if (incremental and obj.exists()
+            and obj.stat().st_mtime >= max(src.stat().st_mtime, _headers_mtime())):
+        return obj, ""
     cmd = [_nvcc(), *ARCH_FLAGS, *COMMON_FLAGS, "-c", str(src), "-o", str(obj)]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
@@ -81,7 +88,9 @@ def build(verbose_ptxas: bool = False, jobs: int | None = None, force: bool = Fa
     jobs = jobs or min(len(sources), os.cpu_count() or 4)
     logs = []
     with concurrent.futures.ThreadPoolExecutor(max_workers=jobs) as pool:
-        results = list(pool.map(lambda s: _compile(s, verbose_ptxas), sources))
+        # unforced builds recompile only the units older than their source or
+        # any header; a forced build recompiles everything
+        results = list(pool.map(lambda s: _compile(s, verbose_ptxas, not force), sources))
     objs = [obj for obj, _ in results]
     logs = [log for _, log in results if log.strip()]
     tmp = OUTPUT.with_suffix(".so.tmp")

@@ -1,7 +1,9 @@
 // Tensor-core fused attention for bf16 / fp16 (dense SDPA and varlen).
 //
 // One CTA owns 128 query rows of one (sequence, head).  Keys are visited in
-// fixed blocks of 128 from the first key of the sequence:
+// fixed blocks of BN from the first key of the sequence (BN = 128, or 64 for
+// D = Dv = 256 so that a two-deep K/V ring fits in shared memory; BN is a
+// function of the head dims only):
 //   warp 0      TMA: Q tile once, then K and V tiles of each key block into a
 //               ring (128-byte swizzle; V is read N-major for the PV product).
 //   warp 1      MMA: S_j = Q K_j^T (tcgen05, M=128, N=128, fp32 in TMEM, two S
@@ -60,17 +62,20 @@ struct AttnTcParams {
   int* status;
 };
 
-// Shared memory plan.  HALVES = 2 splits every query row between two softmax
-// warps (64 score columns each) that exchange partial max / sum through kX;
-// the largest head sizes (256/256) keep one warp per row to fit 227 KB.
+// Key block of the one-tile kernel for padded head dims (DP, DVP).
 template <int DP, int DVP>
+constexpr int at_block_n() { return (DP == 256 && DVP == 256) ? 64 : kAtBN; }
+
+// Shared memory plan.  HALVES = 2 splits every query row between two softmax
+// warps (BN/2 score columns each) that exchange partial max / sum through kX.
+template <int DP, int DVP, int BN = at_block_n<DP, DVP>()>
 struct AttnSmem {
   static constexpr uint32_t kQ = kAtBM * DP * 2;
-  static constexpr uint32_t kK = kAtBN * DP * 2;
-  static constexpr uint32_t kV = kAtBN * DVP * 2;
-  static constexpr uint32_t kP = kAtBM * kAtBN * 2;
+  static constexpr uint32_t kK = BN * DP * 2;
+  static constexpr uint32_t kV = BN * DVP * 2;
+  static constexpr uint32_t kP = kAtBM * BN * 2;
   static constexpr uint32_t kBar = 256;
-  static constexpr int kHalves = (DP == 256 && DVP == 256) ? 1 : 2;
+  static constexpr int kHalves = 2;
   static constexpr uint32_t kX = kHalves == 2 ? 2 * 2 * 128 * 4 : 0;
   static constexpr uint32_t kFixed = 1024 + kQ + kP + kBar + kX;
   static constexpr int kStages = (227u * 1024u - kFixed) / (kK + kV) >= 2 ? 2 : 1;
@@ -203,12 +208,14 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
   using L = AttnSmem<DP, DVP>;
+  constexpr int BN = at_block_n<DP, DVP>();  // keys per block
   constexpr int S = L::kStages;
   constexpr int HALVES = L::kHalves;
-  constexpr int CPT = 4 / HALVES;  // 32-column score chunks per softmax thread
+  constexpr int CPT = BN / 32 / HALVES;  // 32-column score chunks per softmax thread
   constexpr int kQChunks = DP / 64;
   constexpr int kVChunks = DVP / 64;
-  constexpr uint32_t kIdescS = idesc_f16(AtFmt<T>::v, kAtBM, kAtBN, false, false);
+  constexpr uint32_t kKChunk = BN * 128;  // one 64-column chunk of a K block
+  constexpr uint32_t kIdescS = idesc_f16(AtFmt<T>::v, kAtBM, BN, false, false);
   constexpr uint32_t kIdescO = idesc_f16(AtFmt<T>::v, kAtBM, DVP, false, true);
   constexpr uint32_t kOCol = 256;  // TMEM: S0 [0,128), S1 [128,256), O [256, 256+DVP)
 
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
   int64_t kend_cta = lk_seq;
   if (p.causal != 0) kend_cta = min(lk_seq, q0 + nrows - 1 + shift + 1);
   if (kend_cta < 0) kend_cta = 0;
-  const int nblk = static_cast<int>((kend_cta + kAtBN - 1) / kAtBN);
+  const int nblk = static_cast<int>((kend_cta + BN - 1) / BN);
 
   // per-row output pointer (softmax warps)
   const int r = (warp & 3) * 32 + lane;
@@ -344,17 +351,17 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
       for (int jb = 0; jb < nblk; ++jb) {
         const int stage = jb % S;
         const uint32_t ph = static_cast<uint32_t>(jb / S) & 1u;
-        const int row = kc0 + jb * kAtBN;
+        const int row = kc0 + jb * BN;
         if (!at_wait(&k_empty[stage], ph ^ 1u, abort_flag, p.status)) break;
         mbar_arrive_expect_tx(&k_full[stage], L::kK);
         uint8_t* k_dst = sK + stage * L::kK;
         for (int c = 0; c < kQChunks; ++c)
-          tma_load_4d(k_dst + c * 16384, &tmK, &k_full[stage], c * 64, row, hkc, bc);
+          tma_load_4d(k_dst + c * kKChunk, &tmK, &k_full[stage], c * 64, row, hkc, bc);
         k_issued = jb + 1;
         if (!at_wait(&v_empty[stage], ph ^ 1u, abort_flag, p.status)) break;
         mbar_arrive_expect_tx(&v_full[stage], L::kV);
         uint8_t* v_dst = sV + stage * L::kV;
-        for (int kcnk = 0; kcnk < 2; ++kcnk)
+        for (int kcnk = 0; kcnk < BN / 64; ++kcnk)
           for (int nc = 0; nc < kVChunks; ++nc)
             tma_load_4d(v_dst + (kcnk * kVChunks + nc) * 8192, &tmV, &v_full[stage], nc * 64,
                         row + kcnk * 64, hkc, bc);
@@ -387,9 +394,10 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
         const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + stage * L::kK);
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16(tmem + static_cast<uint32_t>(sb * 128), smem_desc_sw128(qa + off, 16, 1024),
-                   smem_desc_sw128(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+          const uint32_t qoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * kKChunk + (kk & 3) * 32;
+          umma_f16(tmem + static_cast<uint32_t>(sb * 128), smem_desc_sw128(qa + qoff, 16, 1024),
+                   smem_desc_sw128(ka + koff, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
         umma_commit(&k_empty[stage]);  // K_jb is free once S_jb is done
@@ -407,7 +415,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
         tc_fence_after();
         const uint32_t pa = smem_u32(sP), va = smem_u32(sV + stage * L::kV);
 #pragma unroll
-        for (int kk = 0; kk < kAtBN / 16; ++kk) {
+        for (int kk = 0; kk < BN / 16; ++kk) {
           const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
           const uint32_t boff = (kk >> 2) * (kVChunks * 8192) + (kk & 3) * 2048;
           umma_f16(tmem + kOCol, smem_desc_sw128(pa + aoff, 16, 1024),
@@ -466,9 +474,9 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t col0 = static_cast<int64_t>(jb) * kAtBN;
+      const int64_t col0 = static_cast<int64_t>(jb) * BN;
       const int nvis = static_cast<int>(max(static_cast<int64_t>(0),
-                                            min(static_cast<int64_t>(kAtBN), kr - col0)));
+                                            min(static_cast<int64_t>(BN), kr - col0)));
       const uint32_t s_addr = tmem + lane_base + static_cast<uint32_t>(sb * 128);
       // ---- pass 1: this thread's CPT chunks of 32 scores stay in registers;
       // maximum of the scaled, masked scores (fixed tree within each chunk,
@@ -594,11 +602,11 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
       }
       // Zero V rows of a partial block that lie past the sequence end (they
       // may belong to the next packed sequence).
-      if (p.varlen && col0 + kAtBN > lk_seq) {
+      if (p.varlen && col0 + BN > lk_seq) {
         const int stage = jb % S;
         uint8_t* vt = sV + stage * L::kV;
         const int first = static_cast<int>(lk_seq - col0);
-        for (int row = first + st; row < kAtBN; row += 128 * HALVES) {
+        for (int row = first + st; row < BN; row += 128 * HALVES) {
           const int kcnk = row >> 6, rr = row & 63;
           for (int nc = 0; nc < kVChunks; ++nc) {
             uint4* dst = reinterpret_cast<uint4*>(vt + (kcnk * kVChunks + nc) * 8192 + rr * 128);
@@ -1517,8 +1525,12 @@ int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream) {
     tk = tq;
     tv = tq;
   } else {
+    // K rows per box = the key block of the kernel that runs
+    const uint32_t kbox = (!use_two_tiles(dp, dvp, a, varlen) && dp == 256 && dvp == 256)
+                              ? static_cast<uint32_t>(bio::at_block_n<256, 256>())
+                              : static_cast<uint32_t>(bio::kAtBN);
     if (!at_map(&tk, a->dtype, a->k, a->d, a->lk, a->kv_heads, nb, a->k_st, a->k_sh, a->k_sb,
-                64, bio::kAtBN))
+                64, kbox))
       return BIO_ERR_ALIGN;
     if (!at_map(&tv, a->dtype, a->v, a->dv, a->lk, a->kv_heads, nb, a->v_st, a->v_sh, a->v_sb,
                 64, 64))
