@@ -59,6 +59,11 @@ struct AttnTcParams {
   int64_t nseq;
   const int* blk_start;
   const int* order;  // two-tile varlen: planned position -> sequence id
+  // One-tile dense kernel, grouped-query packing (0 = off): a CTA's 128 rows
+  // are pack_tok consecutive query tokens of each of the 128 / pack_tok query
+  // heads that share KV head blockIdx.y (row r: head blockIdx.y * 128 /
+  // pack_tok + r / pack_tok, token blockIdx.x * pack_tok + r % pack_tok).
+  int pack_tok;
   int* status;
 };
 
@@ -223,6 +228,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   // ---------------------------------------------------------------- work
+  const int pt = p.varlen ? 0 : p.pack_tok;
   int64_t b = 0, h = blockIdx.y, q0, lq_seq, lk_seq, q_tok0, k_tok0;
   if (p.varlen) {
     const int64_t g = blockIdx.x;
@@ -250,27 +256,35 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
     k_tok0 = ks0;
   } else {
     b = blockIdx.z;
-    q0 = static_cast<int64_t>(blockIdx.x) * kAtBM;
+    if (pt > 0) {
+      q0 = static_cast<int64_t>(blockIdx.x) * pt;
+      h = static_cast<int64_t>(blockIdx.y) * (kAtBM / pt);  // first query head of the tile
+    } else {
+      q0 = static_cast<int64_t>(blockIdx.x) * kAtBM;
+    }
     lq_seq = p.lq;
     lk_seq = p.lk;
     q_tok0 = q0;
     k_tok0 = 0;
   }
-  const int64_t hk = h / (p.heads / p.kv_heads);
-  const int64_t nrows = min(static_cast<int64_t>(kAtBM), lq_seq - q0);
+  const int64_t hk = pt > 0 ? static_cast<int64_t>(blockIdx.y) : h / (p.heads / p.kv_heads);
+  // query tokens of this tile that exist (each packed head has the same ones)
+  const int64_t nrows = min(static_cast<int64_t>(pt > 0 ? pt : kAtBM), lq_seq - q0);
   const int64_t shift = (p.causal == 2) ? (lk_seq - lq_seq) : 0;
   int64_t kend_cta = lk_seq;
   if (p.causal != 0) kend_cta = min(lk_seq, q0 + nrows - 1 + shift + 1);
   if (kend_cta < 0) kend_cta = 0;
   const int nblk = static_cast<int>((kend_cta + BN - 1) / BN);
 
-  // per-row output pointer (softmax warps)
+  // per-row head, token and output pointer (softmax warps)
   const int r = (warp & 3) * 32 + lane;
-  const int64_t i = q0 + r;
-  const bool row_valid = warp >= 2 && r < nrows;
+  const int rt = pt > 0 ? (r % pt) : r;              // token offset of row r in the tile
+  const int64_t hrow = pt > 0 ? h + r / pt : h;      // query head of row r
+  const int64_t i = q0 + rt;
+  const bool row_valid = warp >= 2 && rt < nrows;
   T* out_row = nullptr;
   if (row_valid) {
-    out_row = static_cast<T*>(p.o) + (p.varlen ? 0 : b * p.o_sb) + h * p.o_sh +
+    out_row = static_cast<T*>(p.o) + (p.varlen ? 0 : b * p.o_sb) + hrow * p.o_sh +
               (p.varlen ? (q_tok0 + r) : i) * p.o_st;
   }
   if (nblk == 0) {
@@ -439,7 +453,7 @@ __global__ void __launch_bounds__(AttnSmem<DP, DVP>::kThreads, 1)
     if (p.causal != 0) kr = min(lk_seq, i + shift + 1);
     if (!row_valid || kr < 0) kr = 0;
     const int64_t mrow = (p.mask_kind != 0 && row_valid)
-                             ? b * p.m_sb + h * p.m_sh + i * p.m_sq
+                             ? b * p.m_sb + hrow * p.m_sh + i * p.m_sq
                              : 0;
     // Without masks and with a positive scale, max(s * scale) == max(s) * scale
     // exactly (rounding is monotonic), so the hot loop runs on raw scores.
@@ -1389,7 +1403,7 @@ std::mutex g_at_mu;
 // stride.  Returns false when a stride is not TMA-expressible.
 bool at_map(CUtensorMap* map, int dtype, const void* ptr, int64_t dim, int64_t tokens,
             int64_t heads, int64_t batch, int64_t s_tok, int64_t s_head, int64_t s_batch,
-            uint32_t box0, uint32_t box1) {
+            uint32_t box0, uint32_t box1, uint32_t box2 = 1) {
   bio_host::EncodeTiledFn enc = bio_host::encode_tiled_fn();
   if (enc == nullptr) return false;
   const uint64_t es = 2;
@@ -1405,7 +1419,7 @@ bool at_map(CUtensorMap* map, int dtype, const void* ptr, int64_t dim, int64_t t
   st[2] = fix(batch, s_batch, st[1] * static_cast<uint64_t>(heads));
   for (int i = 0; i < 3; ++i)
     if (st[i] % 16 != 0 || st[i] == 0 || st[i] >= (1ull << 40)) return false;
-  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t box[4] = {box0, box1, box2, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt =
       dtype == BIO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1437,9 +1451,11 @@ int launch_at(const bio_attn_args* a, bool varlen, const CUtensorMap& q, const C
     if (g > 2147483647) return BIO_ERR_SHAPE;
     grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads), 1);
   } else {
-    const int64_t g = (a->lq + bio::kAtBM - 1) / bio::kAtBM;
-    if (g > 2147483647 || a->batch > 65535 || a->heads > 65535) return BIO_ERR_SHAPE;
-    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(a->heads),
+    const int64_t span = p.pack_tok > 0 ? p.pack_tok : bio::kAtBM;  // tokens per tile
+    const int64_t g = (a->lq + span - 1) / span;
+    const int64_t gy = p.pack_tok > 0 ? a->kv_heads : a->heads;
+    if (g > 2147483647 || a->batch > 65535 || gy > 65535) return BIO_ERR_SHAPE;
+    grid = dim3(static_cast<unsigned>(g), static_cast<unsigned>(gy),
                 static_cast<unsigned>(a->batch));
   }
   kern<<<grid, L::kThreads, L::kTotal, s>>>(q, k, v, p);
@@ -1516,9 +1532,20 @@ int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream) {
   if (!al16(a->q) || !al16(a->k) || !al16(a->v)) return BIO_ERR_ALIGN;
   const int dp = pad64(a->d), dvp = pad64(a->dv);
   const int64_t nb = varlen ? 1 : a->batch;
+  // Grouped-query packing of the one-tile dense kernel: the query heads that
+  // share a KV head fill one 128-row tile together (group of 2..16 heads,
+  // 128 / group tokens each), so short queries do not leave most rows idle
+  // and the group's K/V blocks are read once.  A row's arithmetic does not
+  // depend on the tile it lands in, so this changes no bit.
+  const int64_t grp = a->kv_heads > 0 ? a->heads / a->kv_heads : 0;
+  const bool pack = !varlen && !use_two_tiles(dp, dvp, a, varlen) && a->kv_heads > 0 &&
+                    a->heads % a->kv_heads == 0 &&
+                    (grp == 2 || grp == 4 || grp == 8 || grp == 16);
+  const int pack_tok = pack ? static_cast<int>(bio::kAtBM / grp) : 0;
   CUtensorMap tq, tk, tv;
   if (!at_map(&tq, a->dtype, a->q, a->d, a->lq, a->heads, nb, a->q_st, a->q_sh, a->q_sb, 64,
-              bio::kAtBM))
+              pack ? static_cast<uint32_t>(pack_tok) : bio::kAtBM,
+              pack ? static_cast<uint32_t>(grp) : 1u))
     return BIO_ERR_ALIGN;
   if (a->lk == 0) {
     // no key at all: every row is zero and K/V are never read
@@ -1566,6 +1593,7 @@ int attn_tc_launch(const bio_attn_args* a, bool varlen, void* stream) {
   p.blk_start = static_cast<const int*>(a->workspace);
   p.order = a->workspace != nullptr ? static_cast<const int*>(a->workspace) + a->nseq + 1
                                     : nullptr;
+  p.pack_tok = pack_tok;
   p.status = bio_host::status_word(a->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool two = use_two_tiles(dp, dvp, a, varlen);
