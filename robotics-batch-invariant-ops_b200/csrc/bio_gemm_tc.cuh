@@ -334,33 +334,35 @@ __device__ __forceinline__ void scatter_chunk(const TcGemmParams& p, T* cb, int 
 
 // Bias of an epilogue tile, loaded before the accumulator is ready so that
 // its memory latency overlaps the main loop: lane l holds the column bias of
-// column nbase + 32 c + l in col[c] (0 past N), and the row bias of its own
-// output row m in row (BIAS_PER_ROW, 0 past M).  The scatter mode keeps its
-// own per-channel bias path.
-template <typename T, int NC>
+// column nbase + l in col0 and nbase + 32 + l in col1 (the first two 32-column
+// chunks; 0 past N; later chunks are fetched one chunk pair ahead inside
+// epi_tile), and the row bias of its own output row m in row (BIAS_PER_ROW,
+// 0 past M).  The scatter mode keeps its own per-channel bias path.
 struct EpiBias {
-  float col[NC];
+  float col0, col1;
   float row;
   bool has;
 };
 
-template <typename T, int NC>
-__device__ __forceinline__ EpiBias<T, NC> epi_bias_load(const TcGemmParams& p, const T* bias_b,
-                                                       int nbase, int m, int rows, int lane) {
-  EpiBias<T, NC> eb;
+template <typename T>
+__device__ __forceinline__ float epi_bias_col(const TcGemmParams& p, const T* bias_b, int n) {
+  return n < p.n ? to_f32(bias_b[n]) : 0.f;
+}
+
+template <typename T>
+__device__ __forceinline__ EpiBias epi_bias_load(const TcGemmParams& p, const T* bias_b, int nbase,
+                                                 int m, int rows, int lane) {
+  EpiBias eb;
   eb.has = bias_b != nullptr && !p.scatter;
   eb.row = 0.f;
-#pragma unroll
-  for (int c = 0; c < NC; ++c) eb.col[c] = 0.f;
+  eb.col0 = 0.f;
+  eb.col1 = 0.f;
   if (!eb.has) return eb;
   if (p.bias_per_row) {
     eb.row = m < rows ? to_f32(bias_b[m]) : 0.f;
   } else {
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int n = nbase + c * 32 + lane;
-      eb.col[c] = n < p.n ? to_f32(bias_b[n]) : 0.f;
-    }
+    eb.col0 = epi_bias_col<T>(p, bias_b, nbase + lane);
+    eb.col1 = epi_bias_col<T>(p, bias_b, nbase + 32 + lane);
   }
   return eb;
 }
@@ -446,15 +448,17 @@ __device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uin
 // TMEM columns of its 32 lanes starting at tbase (output columns from
 // nbase), loaded with the next chunk's load in flight while the current one
 // is converted, then stored through the tensor-store staging (c_tma; NBUF
-// 2 KB buffers at `stage`) or directly.  The chunk loop is unrolled so each
-// chunk's prefetched bias sits in a register.
+// 2 KB buffers at `stage`) or directly.  The chunk loop is rolled two chunks
+// at a time (compact code: a launch's first tile runs from a cold
+// instruction cache), with the next pair's column bias fetched one pair
+// ahead.
 template <typename T, int NCH, int NBUF>
 __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMap* tmC,
                                          uint32_t tbase, T* crow, int m, int rows, int nbase,
-                                         const T* bias_b, const EpiBias<T, NCH>& eb,
-                                         uint8_t* stage, int lane, int& epi_k, int b1, int b2) {
+                                         const T* bias_b, const EpiBias& eb, uint8_t* stage,
+                                         int lane, int& epi_k, int b1, int b2) {
   const int mrow0 = m - lane;  // first output row of this warp
-  auto emit = [&](const uint32_t(&rr)[32], int c) {
+  auto emit = [&](const uint32_t(&rr)[32], int c, float bcol) {
     const int n0 = nbase + 32 * c;
     if (p.c_tma) {
       uint8_t* buf = stage + (NBUF == 2 ? (epi_k & 1) * 2048 : 0);
@@ -462,7 +466,7 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
         if (lane == 0) bulk_wait_read<NBUF - 1>();
         __syncwarp();
       }
-      epi_chunk_stage<T>(p, rr, buf, eb.has, eb.col[c], eb.row, lane);
+      epi_chunk_stage<T>(p, rr, buf, eb.has, bcol, eb.row, lane);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -471,26 +475,36 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
       }
       ++epi_k;
     } else {
-      epi_chunk<T>(p, rr, crow, m, rows, n0, bias_b, eb.has, eb.col[c], eb.row);
+      epi_chunk<T>(p, rr, crow, m, rows, n0, bias_b, eb.has, bcol, eb.row);
     }
   };
   if constexpr (NCH == 1) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tbase, r);
     tmem_ld_wait_tied(r);
-    emit(r, 0);
+    emit(r, 0, eb.col0);
   } else {
+    static_assert(NCH % 2 == 0, "chunk pairs");
+    const bool col_bias = eb.has && !p.bias_per_row;
+    float bc0 = eb.col0, bc1 = eb.col1;
     uint32_t ra[32], rb[32];
     tmem_ld_32x32b_x32(tbase, ra);
     tmem_ld_wait_tied(ra);
-#pragma unroll
+#pragma unroll 1
     for (int c = 0; c < NCH; c += 2) {
+      float nb0 = 0.f, nb1 = 0.f;
+      if (col_bias && c + 2 < NCH) {
+        nb0 = epi_bias_col<T>(p, bias_b, nbase + 32 * (c + 2) + lane);
+        nb1 = epi_bias_col<T>(p, bias_b, nbase + 32 * (c + 3) + lane);
+      }
       tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 1)), rb);
-      emit(ra, c);
+      emit(ra, c, bc0);
       tmem_ld_wait_tied(rb);
       if (c + 2 < NCH) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 2)), ra);
-      emit(rb, c + 1);
+      emit(rb, c + 1, bc1);
       tmem_ld_wait_tied(ra);
+      bc0 = nb0;
+      bc1 = nb1;
     }
   }
 }
@@ -726,7 +740,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int nbase = ti.nb * BN;
       const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
       // bias loads are issued before the wait: their latency overlaps the main loop
-      const EpiBias<T, BN / 32> eb = epi_bias_load<T, BN / 32>(p, bias_b, nbase, m, sg.rows, lane);
+      const EpiBias eb = epi_bias_load<T>(p, bias_b, nbase, m, sg.rows, lane);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
@@ -978,9 +992,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
       const T* bias_b = bias != nullptr ? bias + ti.b2 * p.bias_s2 : nullptr;
       const int nhalf = ti.nb * BN + h * (BN / 2);  // first output column of this warp
       // bias loads are issued before the wait: their latency overlaps the main loop
-      const EpiBias<T, BN / 64> eb =
-          p.swiglu ? EpiBias<T, BN / 64>{} : epi_bias_load<T, BN / 64>(p, bias_b, nhalf, m,
-                                                                    sg.rows, lane);
+      const EpiBias eb = p.swiglu ? EpiBias{0.f, 0.f, 0.f, false}
+                                  : epi_bias_load<T>(p, bias_b, nhalf, m, sg.rows, lane);
       const bool got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
