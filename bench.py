@@ -1175,7 +1175,7 @@ def main() -> None:
                         help="time the 54 extended VLA operator shapes (ours vs stock)")
     parser.add_argument("--vla", action="store_true",
                         help="config 5: pi0-style VLA step samples/s under the mode")
-    parser.add_argument("--vla-global-batch", type=int, default=128,
+    parser.add_argument("--vla-global-batch", type=int, default=256,
                         help="VLA samples per step over all GPUs (sharded)")
     parser.add_argument("--vla-steps", type=int, default=3, help="timed VLA graph replays")
     parser.add_argument("--no-vla", action="store_true", help="skip the VLA step in the default run")
