@@ -727,10 +727,13 @@ __global__ void attn_plan_kernel(const void* cu_q, int is64, int64_t nseq, int b
 // registers).  The MMA thread issues, per key block j,
 //     PV_0(j), S_0(j+1), PV_1(j), S_1(j+1)
 // so that the tensor core works on one tile while the other tile's softmax
-// runs.  tcgen05 operations of one thread complete in issue order, so the
-// arrival of S_t(j+1) also tells softmax t that PV_t(j) is done: its P
-// buffer may be rewritten and its O row rescaled.  K and V have separate
-// rings (K is consumed early by the S products, V late by the PV products).
+// runs.  The softmax writes P_t (rounded to the input dtype, two per 32-bit
+// column) over the first 64 columns of S_t in TMEM, and PV_t reads it from
+// there as its A operand (no shared-memory P tile, no proxy fence); S_t(j+1)
+// then overwrites it.  tcgen05 operations of one thread complete in issue
+// order, so the arrival of S_t(j+1) also tells softmax t that PV_t(j) is
+// done: its O row may be rescaled.  K and V have separate rings (K is
+// consumed early by the S products, V late by the PV products).
 //
 // Per-row arithmetic is the same as in attn_tc_kernel's contract: keys in
 // fixed blocks of 128 from the first key of the sequence, a fixed tree per 32
@@ -794,11 +797,10 @@ struct Attn2Smem {
   static constexpr uint32_t kQ = 128 * D * 2;  // one tile
   static constexpr uint32_t kK = kAtBN * D * 2;
   static constexpr uint32_t kV = kAtBN * D * 2;
-  static constexpr uint32_t kP = 128 * kAtBN * 2;  // one tile
   static constexpr int kKS = D == 128 ? 2 : 4;
-  static constexpr int kVS = D == 128 ? 1 : 4;
+  static constexpr int kVS = D == 128 ? 2 : 4;
   static constexpr uint32_t kBar = 256;
-  static constexpr uint32_t kTotal = 1024 + 2 * kQ + 2 * kP + kKS * kK + kVS * kV + kBar;
+  static constexpr uint32_t kTotal = 1024 + 2 * kQ + kKS * kK + kVS * kV + kBar;
   static_assert(kTotal <= 227u * 1024u, "attention smem plan exceeds 227 KB");
 };
 
@@ -981,8 +983,7 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;                 // [2][kQ]
-  uint8_t* sP = sQ + 2 * L::kQ;       // [2][kP]
-  uint8_t* sK = sP + 2 * L::kP;       // [KS][kK]
+  uint8_t* sK = sQ + 2 * L::kQ;       // [KS][kK]
   uint8_t* sV = sK + KS * L::kK;      // [VS][kV]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * L::kV);
   uint64_t* q_full = bars;
@@ -1104,13 +1105,15 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
         if (!at_wait(&v_full[vs], static_cast<uint32_t>(jb / VS) & 1u, abort_flag, p.status))
           return false;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP + t * L::kP), va = smem_u32(sV + vs * L::kV);
+        const uint32_t va = smem_u32(sV + vs * L::kV);
+        // P_t is the A operand straight from TMEM (the first 64 columns of
+        // S_t, 8 columns per K = 16 step)
+        const uint32_t pa = tmem + static_cast<uint32_t>(t * 128);
 #pragma unroll
         for (int kk = 0; kk < kAtBN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
           const uint32_t boff = (kk >> 2) * (kChunks * 8192) + (kk & 3) * 2048;
-          umma_f16(tmem + 256u + static_cast<uint32_t>(t * D), smem_desc_sw128(pa + aoff, 16, 1024),
-                   smem_desc_sw128(va + boff, 8192, 1024), kIdescO, (jb | kk) != 0 ? 1u : 0u);
+          umma_f16_ts(tmem + 256u + static_cast<uint32_t>(t * D), pa + static_cast<uint32_t>(8 * kk),
+                      smem_desc_sw128(va + boff, 8192, 1024), kIdescO, (jb | kk) != 0 ? 1u : 0u);
         }
         if (jb == (t == 0 ? nblk0 : nblk1) - 1) umma_commit(&o_done[t]);
         return true;
@@ -1152,7 +1155,6 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
     const float cexp = plain ? p.scale * kLog2e : kLog2e;  // exponent factor of the domain
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* sPt = sP + t * L::kP;
     for (int jb = 0; jb < my_nblk; ++jb) {
       const bool got = at_wait(&s_full[t], static_cast<uint32_t>(jb) & 1u, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) {
@@ -1270,10 +1272,9 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
         if (c + 1 < 4) tmem_ld_32x32b_x32(s_addr + static_cast<uint32_t>((c + 1) * 32), fn);
         clip_chunk(f, c);
         uint64_t acc = f2_pack(0.f, 0.f);
-        uint8_t* base = sPt + (c >> 1) * 16384 + r * 128;
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
-          uint32_t w4[4];
+          uint32_t w4[4];  // 8 rounded probabilities, two per word
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = u4 * 8 + 2 * e;
@@ -1295,15 +1296,17 @@ __global__ void __launch_bounds__(kAt2Threads, 1)
             w4[e] = pack_pair<T>(x0, x1);
             acc = f2_add(acc, f2_pack(x0, x1));
           }
-          const int u = (c & 1) * 4 + u4;
-          *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) =
-              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          // P chunk c -> TMEM columns [16 c, 16 c + 16) of S_t, which hold
+          // S chunk c / 2: already read into registers (chunks run in order)
+          tmem_st_32x32b_x4(s_addr + static_cast<uint32_t>(16 * c + 4 * u4), w4[0], w4[1],
+                            w4[2], w4[3]);
         }
         float s0, s1;
         f2_unpack(acc, s0, s1);
         lsum += s0 + s1;
         if (c + 1 < 4) tmem_ld_wait();
       }
+      tmem_st_wait();  // P_t is in TMEM before the PV product is released
       if (m_new != -INFINITY) {
         l = l * alpha + lsum;
         m = m_new;

@@ -240,6 +240,20 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// tcgen05.mma (M=128, kind::f16) with A read from tensor memory: row i of A in
+// lane i, the K = 16 elements of the instruction packed two per 32-bit
+// column (elements 2c and 2c+1 of a row in the low and high half of column
+// c), so one instruction reads 8 columns from a_tmem; B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -283,6 +297,25 @@ __device__ __forceinline__ void tmem_ld_wait_tied(uint32_t (&r)[32]) {
                  "+r"(r[30]), "+r"(r[31])
                :
                : "memory");
+}
+
+// Store 32 lanes x 4 consecutive 32-bit columns to TMEM.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t r0, uint32_t r1,
+                                                  uint32_t r2, uint32_t r3) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+               : "memory");
+}
+
+// Store 32 lanes x 16 consecutive 32-bit columns to TMEM.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
 }
 
 // Store 32 lanes x 32 consecutive 32-bit columns to TMEM (inverse of
