@@ -1121,6 +1121,22 @@ def run_profile_point(args) -> None:
     sys.path.insert(0, str(PKG_ROOT))
     from batch_invariant_ops import linear_batch_invariant, scaled_dot_product_attention_batch_invariant
 
+    if args.profile_point.startswith("gated:"):
+        # fused GeGLU GEMM and the plain GEMM of the same operands, per round
+        from batch_invariant_ops import gated_linear_batch_invariant
+
+        m, f, k = (int(v) for v in args.profile_point[6:].split("x"))
+        dev = torch.device("cuda", 0)
+        gen = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+        w = (torch.randn(2 * f, k, device=dev, generator=gen) / math.sqrt(k)).to(torch.bfloat16)
+        for _ in range(1 + args.steps):
+            y = gated_linear_batch_invariant(x, w)
+            linear_batch_invariant(x, w)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_point": args.profile_point, "launches": 2 * (1 + args.steps),
+                          "checksum": float(y.float().sum().item())}))
+        return
     if args.profile_point.startswith("attn:"):
         bsz, seq, causal = (int(v) for v in args.profile_point[5:].split(","))
         dev = torch.device("cuda", 0)
