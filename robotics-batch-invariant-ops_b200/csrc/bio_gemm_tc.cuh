@@ -758,8 +758,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    // tensor stores must finish before the CTA (and its staging) goes away
-    if (p.c_tma && lane == 0) bulk_wait_all();
+    // tensor stores must have read their staging before the CTA's shared
+    // memory goes away; their global writes complete with the grid
+    if (p.c_tma && lane == 0) bulk_wait_read<0>();
   }
 
   tc_fence_before();
@@ -1068,8 +1069,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    // tensor stores must finish before the CTA (and its staging) goes away
-    if (p.c_tma && lane == 0) bulk_wait_all();
+    // tensor stores must have read their staging before the CTA's shared
+    // memory goes away; their global writes complete with the grid
+    if (p.c_tma && lane == 0) bulk_wait_read<0>();
   }
 
   // Abort path: give loads already issued (which count on the leader's
