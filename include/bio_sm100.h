@@ -155,8 +155,8 @@ BIO_API int bio_gemm_f32_exact(const bio_gemm_args* args, void* workspace,
                                int64_t workspace_bytes, void* stream);
 
 /* bio_gemm with an explicit output tile for the tensor-core path (f16/bf16):
- * tile_m 128 (one CTA) or 256 (CTA pair), tile_n 32/64/128/256 (pair: 128 or
- * 256; an N-contiguous B needs tile_n >= 64).  The per-element arithmetic of
+ * tile_m 128 (one CTA) or 256 (CTA pair), tile_n 32/64/96/128/256 (pair: 128
+ * or 256; an N-contiguous B needs tile_n 64, 128 or 256).  The per-element arithmetic of
  * every tile is the same sequence (64-wide K blocks in increasing order, four
  * K=16 MMAs per block into an fp32 accumulator, one rounding), so all tiles
  * must produce identical bits; tests use this entry to check exactly that.

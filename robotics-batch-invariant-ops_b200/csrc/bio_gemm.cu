@@ -339,7 +339,7 @@ int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v) 
   if (!tile_supported(tc)) return BIO_ERR_ARG;
   // An N-contiguous B is staged in 64-column swizzle atoms: tiles narrower
   // than one atom are not built for it.
-  if (b_mn && !tc.pair && tc.bn < 64) return BIO_ERR_ARG;
+  if (b_mn && !tc.pair && (tc.bn < 64 || tc.bn == 96)) return BIO_ERR_ARG;
   if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn);
   return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn);
 }
@@ -401,7 +401,7 @@ int grouped_impl(const bio_gemm_args* a, const int32_t* seg, const void* up, voi
   // tile gives the same bits
   TileChoice tc = pick_tile((a->m + a->batch1 - 1) / a->batch1, a->n, a->batch1,
                             bio_host::sm_count(a->device));
-  if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
+  tc = for_layout(tc, b_mn);
   if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn, seg);
   return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn, seg);
 }
@@ -488,7 +488,7 @@ int bio_conv_transpose(int32_t dtype, const void* x, const void* w, const void* 
   sc.o1o2 = g->in[1] * g->kernel[1] * g->in[2] * g->kernel[2];
   sc.vec = aligned16(y);
   TileChoice tc = pick_tile(p_in, n, nb * groups, bio_host::sm_count(device));
-  if (!tc.pair && tc.bn < 64) tc.bn = 64;  // N-contiguous B: 64-column atoms
+  tc = for_layout(tc, true);  // N-contiguous B: whole 64-column atoms
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (dtype == BIO_BF16)
     return dispatch_tc<__nv_bfloat16>(&a, tc, stream, true, true, nullptr, &sc);

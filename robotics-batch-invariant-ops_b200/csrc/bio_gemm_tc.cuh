@@ -484,18 +484,18 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
     tmem_ld_wait_tied(r);
     emit(r, 0, eb.col0);
   } else {
-    static_assert(NCH % 2 == 0, "chunk pairs");
+    // pairs of chunks, then (odd NCH) one last chunk already loaded into ra
     const bool col_bias = eb.has && !p.bias_per_row;
     float bc0 = eb.col0, bc1 = eb.col1;
     uint32_t ra[32], rb[32];
     tmem_ld_32x32b_x32(tbase, ra);
     tmem_ld_wait_tied(ra);
 #pragma unroll 1
-    for (int c = 0; c < NCH; c += 2) {
+    for (int c = 0; c + 1 < NCH; c += 2) {
       float nb0 = 0.f, nb1 = 0.f;
       if (col_bias && c + 2 < NCH) {
         nb0 = epi_bias_col<T>(p, bias_b, nbase + 32 * (c + 2) + lane);
-        nb1 = epi_bias_col<T>(p, bias_b, nbase + 32 * (c + 3) + lane);
+        if (c + 3 < NCH) nb1 = epi_bias_col<T>(p, bias_b, nbase + 32 * (c + 3) + lane);
       }
       tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(32 * (c + 1)), rb);
       emit(ra, c, bc0);
@@ -506,6 +506,7 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
       bc0 = nb0;
       bc1 = nb1;
     }
+    if constexpr (NCH % 2 == 1) emit(ra, NCH - 1, bc0);
   }
 }
 
@@ -545,7 +546,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const __grid_constant__ CUtensorMap tmB5,
                    const __grid_constant__ CUtensorMap tmC, const TcGemmParams p) {
   using L = TcSmem<BN, STAGES>;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  // two accumulator buffers of BN columns; tcgen05.alloc takes a power of two
+  constexpr uint32_t kTmemCols =
+      2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512));
   constexpr uint32_t kIdesc = idesc_f16(TypeFmt<T>::umma, kBM, BN, A_MN, B_MN);
   constexpr uint32_t kBoxBytesMN = 64 * kBK * 2;  // one 64(N) x 64(K) box
 
@@ -1228,9 +1231,22 @@ struct TileChoice {
 
 inline TileChoice pick_tile(int64_t m, int64_t n, int64_t batch, int sms) {
   if (m <= 128) {
-    for (int bn = 128; bn >= 64; bn >>= 1)
-      if (batch * ((n + bn - 1) / bn) * 2 >= sms) return {false, bn};
-    return {false, 32};
+    // One m-block streams B: the width whose waves over the SMs stream the
+    // fewest columns per SM, counting ~16 columns of fixed cost per tile
+    // (N = 11008: 115 tiles of 96 in one wave instead of 86 of 128;
+    // N = 4096: 128 tiles of 32; N = 16384: 128 tiles of 128); ties go to
+    // the wider tile.
+    int best = 128;
+    int64_t best_cost = -1;
+    for (int bn : {128, 96, 64, 32}) {
+      const int64_t tiles = batch * ((n + bn - 1) / bn);
+      const int64_t cost = (tiles + sms - 1) / sms * (bn + 16);
+      if (best_cost < 0 || cost < best_cost) {
+        best = bn;
+        best_cost = cost;
+      }
+    }
+    return {false, best};
   }
   if (n <= 64) return {false, 64};
   const int64_t pair_tiles = batch * ((m + 255) / 256) * ((n + 255) / 256);
@@ -1250,10 +1266,15 @@ inline TileChoice pick_tile(int64_t m, int64_t n, int64_t batch, int sms) {
 
 // The tile bio_gemm runs: pick_tile, widened to one 64-column swizzle atom
 // for an N-contiguous B on the single-CTA path.
-inline TileChoice run_tile(int64_t m, int64_t n, int64_t batch, int sms, bool b_mn) {
-  TileChoice tc = pick_tile(m, n, batch, sms);
+inline TileChoice for_layout(TileChoice tc, bool b_mn) {
+  // an N-contiguous B is staged in whole 64-column swizzle atoms
   if (b_mn && !tc.pair && tc.bn < 64) tc.bn = 64;
+  if (b_mn && !tc.pair && tc.bn == 96) tc.bn = 128;
   return tc;
+}
+
+inline TileChoice run_tile(int64_t m, int64_t n, int64_t batch, int sms, bool b_mn) {
+  return for_layout(pick_tile(m, n, batch, sms), b_mn);
 }
 
 // Configuration reported for (n, k, dtype): the large-M tile and the K block
@@ -1266,7 +1287,7 @@ inline TileChoice reported_tile(int64_t n) {
 template <bool PAIR, int BN>
 constexpr int stages_for() {
   if (PAIR) return BN == 128 ? 8 : 6;
-  return BN <= 64 ? 8 : (BN == 128 ? 6 : 4);
+  return BN <= 64 ? 8 : (BN == 96 ? 7 : (BN == 128 ? 6 : 4));
 }
 
 inline std::mutex g_attr_mu;
@@ -1523,7 +1544,7 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
 // Tile configurations compiled into the library: (pair, bn).
 inline bool tile_supported(const TileChoice& tc) {
   if (tc.pair) return tc.bn == 128 || tc.bn == 256;
-  return tc.bn == 32 || tc.bn == 64 || tc.bn == 128 || tc.bn == 256;
+  return tc.bn == 32 || tc.bn == 64 || tc.bn == 96 || tc.bn == 128 || tc.bn == 256;
 }
 
 // One operand layout and dtype: launches the tile `tc` (b_up: SwiGLU mode,
@@ -1539,6 +1560,11 @@ int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, const int* seg,
   switch (tc.bn) {
     case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
     case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    case 96:
+      // 96 columns are not a whole number of 64-column atoms of an
+      // N-contiguous B
+      if constexpr (B_MN) return BIO_ERR_ARG;
+      else return launch_tc<false, 96, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
     case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
     default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
   }

@@ -67,7 +67,7 @@ def test_k_block_is_fixed_by_dtype(n, dtype):
         assert bm in (128, 256) and bn in (64, 128, 256)
 
 
-BUILT_TILES = {(128, 32), (128, 64), (128, 128), (128, 256), (256, 128), (256, 256)}
+BUILT_TILES = {(128, 32), (128, 64), (128, 96), (128, 128), (128, 256), (256, 128), (256, 256)}
 
 
 @pytest.mark.parametrize("n", (8, 64, 65, 1152, 4096, 11008, 16384, 184622))
@@ -82,7 +82,7 @@ def test_tile_policy_returns_built_tiles(n, b_mn):
             if m <= 128:
                 assert tile[0] == 128, "one m-block runs single-CTA tiles"
             if b_mn and tile[0] == 128:
-                assert tile[1] >= 64, "an N-contiguous B needs a 64-column atom"
+                assert tile[1] in (64, 128, 256), "an N-contiguous B needs whole 64-column atoms"
 
 
 def test_tile_policy_rejects_bad_arguments():

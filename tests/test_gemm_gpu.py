@@ -199,7 +199,7 @@ def test_odd_shapes_and_empty():
 # the tile shape -- one CTA (128 rows) or a CTA pair (256 rows), 32..256
 # columns -- must not change a single bit.  Inputs span 2^-8..2^8 in
 # magnitude so that accumulation order differences would show.
-_TILES_K_MAJOR = ((128, 32), (128, 64), (128, 128), (128, 256), (256, 128), (256, 256))
+_TILES_K_MAJOR = ((128, 32), (128, 64), (128, 96), (128, 128), (128, 256), (256, 128), (256, 256))
 _TILES_N_MAJOR = ((128, 64), (128, 128), (128, 256), (256, 128), (256, 256))
 
 
