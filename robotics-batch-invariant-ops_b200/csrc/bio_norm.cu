@@ -108,9 +108,16 @@ struct NormParams {
   int64_t x_stride, y_stride;  // elements between rows
 };
 
+// Affine parameters of one 8-element group (16-byte loads when aligned, the
+// same values as element loads): `fill` where the parameter is absent.
 template <typename W>
-__device__ __forceinline__ float ld_param(const W* p, int i) {
-  return p != nullptr ? to_f32(p[i]) : 1.f;
+__device__ __forceinline__ void param8(const W* p, int base, int n, float fill, float (&o)[8]) {
+  if (p != nullptr) {
+    norm_load8<W>(p, base, n, o);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = fill;
+  }
 }
 
 // Row held in registers: GPT (groups per thread) groups of 8 per thread.
@@ -177,15 +184,16 @@ __global__ void __launch_bounds__(TEAM == 32 ? 256 : TEAM)
   for (int j = 0; j < GPT; ++j) {
     const int base = (lane_in_team + j * TEAM) * 8;
     if (base >= n) continue;
-    float o[8];
+    float o[8], wv[8], bv[8];
+    param8<W>(w, base, n, 1.f, wv);
+    if constexpr (!RMS) param8<W>(b, base, n, 0.f, bv);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int i = base + e < n ? base + e : n - 1;
       if constexpr (RMS) {
-        o[e] = v[j][e] * rstd * ld_param(w, i);
+        o[e] = v[j][e] * rstd * wv[e];
       } else {
-        const float t = (v[j][e] - mean) * rstd * ld_param(w, i);
-        o[e] = b != nullptr ? t + to_f32(b[i]) : t;
+        const float t = (v[j][e] - mean) * rstd * wv[e];
+        o[e] = b != nullptr ? t + bv[e] : t;
       }
     }
     norm_store8<T>(yr, base, n, o);
@@ -234,13 +242,14 @@ __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
     if (p.rstd_out != nullptr) p.rstd_out[row] = rstd;
   }
   for (int g = threadIdx.x; g < groups; g += TEAM) {
-    float v[8], o[8];
+    float v[8], o[8], wv[8], bv[8];
     norm_load8<T>(xr, g * 8, n, v);
+    param8<W>(w, g * 8, n, 1.f, wv);
+    if constexpr (!RMS) param8<W>(b, g * 8, n, 0.f, bv);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int i = g * 8 + e < n ? g * 8 + e : n - 1;
-      const float t = (v[e] - mean) * rstd * ld_param(w, i);
-      o[e] = (!RMS && b != nullptr) ? t + to_f32(b[i]) : t;
+      const float t = (v[e] - mean) * rstd * wv[e];
+      o[e] = (!RMS && b != nullptr) ? t + bv[e] : t;
     }
     norm_store8<T>(yr, g * 8, n, o);
   }
