@@ -120,6 +120,10 @@ template <typename TI, typename TO, int OP, int TEAM>
 __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
     row_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t rows, int64_t n) {
   constexpr int kTeamsPerBlock = TEAM >= 256 ? 1 : 256 / TEAM;
+  // groups in flight per thread: a 1024-thread team has 64 registers a thread,
+  // so it takes one at a time (the fold order -- a thread's groups in
+  // increasing index -- does not depend on this)
+  constexpr int UNR = TEAM >= 1024 ? 1 : kUnroll;
   __shared__ float scratch[kTeamsPerBlock][TEAM / 32 + 1];
   const int team = threadIdx.x / TEAM;
   const int t = threadIdx.x % TEAM;
@@ -129,13 +133,13 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
     const TI* row = x + r * n;
     if constexpr (OP == kMean || OP == kL2Norm) {
       float acc = 0.f;
-      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
-        float v[kUnroll][8];
+      for (int64_t g0 = t; g0 < groups; g0 += UNR * TEAM) {
+        float v[UNR][8];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < UNR; ++u)
           if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], 0.f);
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < UNR; ++u)
           if (g0 + u * TEAM < groups) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc += (OP == kL2Norm) ? v[u][j] * v[u][j] : v[u][j];
@@ -148,13 +152,13 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
       }
     } else {
       float mx = -INFINITY;
-      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
-        float v[kUnroll][8];
+      for (int64_t g0 = t; g0 < groups; g0 += UNR * TEAM) {
+        float v[UNR][8];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < UNR; ++u)
           if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], -INFINITY);
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < UNR; ++u)
           if (g0 + u * TEAM < groups) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) mx = fmaxf(mx, v[u][j]);
@@ -162,13 +166,13 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
       }
       mx = team_reduce<TEAM, true>(mx, scratch[team]);
       float den = 0.f;
-      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
-        float v[kUnroll][8];
+      for (int64_t g0 = t; g0 < groups; g0 += UNR * TEAM) {
+        float v[UNR][8];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < UNR; ++u)
           if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], -INFINITY);
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < UNR; ++u) {
           const int64_t g = g0 + u * TEAM;
           if (g < groups) {
 #pragma unroll
@@ -187,13 +191,13 @@ __global__ void __launch_bounds__(TEAM >= 256 ? TEAM : 256)
       TO* out = y + r * n;
       const float inv = den != 0.f ? 1.f / den : 0.f;
       const float lse = (OP == kLogSoftmax) ? logf(den) : 0.f;
-      for (int64_t g0 = t; g0 < groups; g0 += kUnroll * TEAM) {
-        float v[kUnroll][8];
+      for (int64_t g0 = t; g0 < groups; g0 += UNR * TEAM) {
+        float v[UNR][8];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < UNR; ++u)
           if (g0 + u * TEAM < groups) load_group(row, g0 + u * TEAM, n, v[u], -INFINITY);
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < UNR; ++u) {
           const int64_t g = g0 + u * TEAM;
           if (g < groups) {
             float o[8];
