@@ -734,6 +734,41 @@ def _ops_cases(api, dev):
     hs = rn(4096, 2048)
     cases.append(("mean dim -1 [4096,2048] bf16", lambda: api.mean_dim(hs, -1), 0,
                   2 * hs.numel() + 2 * 4096, lambda: hs.mean(-1)))
+    # VLA (config 5) shapes: head-dim-256 GQA attention of the action expert
+    # (8 query heads on one KV head, 50 queries over 354 keys) and the
+    # vision tower's head dim 72, both at 128 samples, token-major like the
+    # model's projections
+    for tag, (bsz, h, hk, lq, lk, d) in (("VLA action expert", (128, 8, 1, 50, 354, 256)),
+                                         ("VLA vision tower", (128, 16, 16, 256, 256, 72))):
+        aq = rn(bsz, lq, h, d).transpose(1, 2)
+        ak, av = rn(bsz, lk, hk, d).transpose(1, 2), rn(bsz, lk, hk, d).transpose(1, 2)
+        gq = h != hk
+        cases.append((f"sdpa {tag} B={bsz} H{h}/{hk} Lq={lq} Lk={lk} D{d} bf16",
+                      lambda q=aq, k=ak, v=av, gq=gq:
+                      api.scaled_dot_product_attention_batch_invariant(q, k, v, enable_gqa=gq),
+                      4 * bsz * h * lq * lk * d, 2 * (2 * bsz * h * lq * d + 2 * bsz * hk * lk * d),
+                      lambda q=aq, k=ak, v=av, gq=gq: F.scaled_dot_product_attention(
+                          q, k, v, enable_gqa=gq)))
+    # additions (not in the reference): fused normalisations and the fused
+    # GeGLU projection, against the stock torch ops they replace
+    ln_x, ln_w, ln_b = rn(32768, 1152), rn(1152, scale=0.1) + 1, rn(1152, scale=0.1)
+    cases.append(("layer_norm [32768,1152] bf16 (addition)",
+                  lambda: api.layer_norm_batch_invariant(ln_x, (1152,), ln_w, ln_b), 0,
+                  4 * ln_x.numel(), lambda: F.layer_norm(ln_x, (1152,), ln_w, ln_b)))
+    rm_x, rm_w = rn(38912, 2048), rn(2048, scale=0.1) + 1
+    cases.append(("rms_norm [38912,2048] bf16 (addition)",
+                  lambda: api.rms_norm_batch_invariant(rm_x, (2048,), rm_w, eps=1e-6), 0,
+                  4 * rm_x.numel(), lambda: F.rms_norm(rm_x, (2048,), rm_w, 1e-6)))
+    gx, gw2 = rn(4864, 2048), rn(2 * 16384, 2048, scale=1 / 45)
+
+    def geglu_stock():
+        gate, up = F.linear(gx, gw2).split(16384, dim=-1)
+        return F.gelu(gate, approximate="tanh") * up
+
+    cases.append(("gated_linear GeGLU 4864x2048 -> 16384 bf16 (addition)",
+                  lambda: api.gated_linear_batch_invariant(gx, gw2),
+                  2 * 4864 * 2048 * 2 * 16384, 2 * (gx.numel() + gw2.numel() + 4864 * 16384),
+                  geglu_stock))
     vol = rn(8, 1024, 4, 132, 160)
     cases.append(("vector_norm dim 1 [8,1024,4,132,160] bf16",
                   lambda: api.linalg_vector_norm_batch_invariant(vol, dim=1), 0,
