@@ -118,6 +118,16 @@ typedef struct bio_gemm_args {
 
 BIO_API int bio_gemm(const bio_gemm_args* args, void* stream);
 
+/* bio_gemm followed by a residual add in the epilogue (f16/bf16, one plain
+ * 2-D GEMM: batch1 == batch2 == 1, no flags, c_sn == 1): C = round(round(
+ * alpha A B + bias) + R), the rounding steps of a linear layer followed by
+ * `residual + output`, bit for bit; R is [m, n] with residual_row_stride
+ * (>= n) elements between rows and must not overlap C.  Saves the separate
+ * add's read and write of the GEMM output and its launch.  No counterpart in the reference (a
+ * transformer's residual adds run as stock elementwise ops there). */
+BIO_API int bio_gemm_residual(const bio_gemm_args* args, const void* residual,
+                              int64_t residual_row_stride, void* stream);
+
 /* Configuration id for (n, k, dtype): the large-M output tile and the K block
  * whose fixed order defines every output element's accumulation.  Encodes
  * block_m * 1000000 + block_n * 1000 + block_k.  The output tile of a given

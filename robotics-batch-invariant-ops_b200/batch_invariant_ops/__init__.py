@@ -21,6 +21,7 @@ from .batch_invariant_ops import (
     layer_norm_batch_invariant,
     linalg_vector_norm_batch_invariant,
     linear_batch_invariant,
+    linear_residual_batch_invariant,
     log_softmax,
     matmul_persistent,
     mean_dim,
@@ -61,4 +62,5 @@ __all__ = [
     "layer_norm_batch_invariant",
     "rms_norm_batch_invariant",
     "gated_linear_batch_invariant",
+    "linear_residual_batch_invariant",
 ]

@@ -216,6 +216,7 @@ def _launch(
     segments: torch.Tensor | None = None,
     swiglu_up: Operand | None = None,
     gate_gelu: bool = False,
+    residual: torch.Tensor | None = None,
 ) -> None:
     """Enqueue one GEMM on the current stream of ``c``'s device.
 
@@ -224,7 +225,9 @@ def _launch(
     and C and multiplies them by B batch s.  ``swiglu_up`` (an operand with
     the same layout as ``b``) selects bio_gemm_swiglu: C = silu(A·B) * (A·up)
     with the roundings of separate GEMMs and bio_silu_mul; with ``gate_gelu``
-    the gate activation is GELU-tanh instead of silu (GeGLU).
+    the gate activation is GELU-tanh instead of silu (GeGLU).  ``residual``
+    (a row-contiguous [M, N] tensor of C's dtype) selects bio_gemm_residual:
+    C = residual + (A·B + bias) with the roundings of a linear and an add.
 
     fp32 runs on the int8 tensor cores with exact integer slices
     (bio_gemm_f32_exact, workspace from the caching allocator) whenever that
@@ -295,6 +298,13 @@ def _launch(
                 "bio_gemm_f32_exact",
             )
             return
+    if residual is not None:
+        _lib.check(
+            lib.bio_gemm_residual(ctypes.byref(args), ctypes.c_void_p(residual.data_ptr()),
+                                  residual.stride(0), _lib.stream_of(c)),
+            "bio_gemm_residual",
+        )
+        return
     if tile is None:
         _lib.check(lib.bio_gemm(ctypes.byref(args), _lib.stream_of(c)), "bio_gemm")
     else:
@@ -352,6 +362,28 @@ def gated(x: torch.Tensor, weight: torch.Tensor, gelu: bool) -> torch.Tensor | N
         return None
     launch(opa, opg, out, batch1=1, batch2=1, m=m, n=f, k=k, c_sm=f, c_sn=1, c_s1=0, c_s2=0,
            swiglu_up=opu, gate_gelu=gelu)
+    return out
+
+
+def linear_residual(r: torch.Tensor, x: torch.Tensor, w: torch.Tensor,
+                    bias: torch.Tensor | None) -> torch.Tensor | None:
+    """r + (x @ w^T + bias) for r [M, N], x [M, K], w [N, K] (f16/bf16) in one
+    GEMM (bio_gemm_residual); None when the residual's rows are not
+    contiguous."""
+    m, k = x.shape
+    n = w.shape[0]
+    if r.stride(-1) != 1 or (m > 1 and r.stride(0) < n):
+        return None
+    out = torch.empty((m, n), device=x.device, dtype=x.dtype)
+    if m == 0 or n == 0:
+        return out
+    if bias is not None:
+        bias = bias.to(x.dtype).contiguous()
+    b = w.t()
+    opa = operand_a(x, 1, 1, m, k, x.stride(0), x.stride(1), 0, 0)
+    opb = operand_b(b, 1, 1, k, n, b.stride(0), b.stride(1), 0, 0)
+    launch(opa, opb, out, batch1=1, batch2=1, m=m, n=n, k=k, c_sm=n, c_sn=1, c_s1=0, c_s2=0,
+           bias=bias, residual=r)
     return out
 
 

@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "bio_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "bio_clear_device_status": (ctypes.c_int, [ctypes.c_int]),
     "bio_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P]),
+    "bio_gemm_residual": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _P, _I64, _P]),
     "bio_gemm_tile_config": (ctypes.c_int, [_I64, _I64, _I32]),
     "bio_gemm_tile_for": (
         ctypes.c_int,

@@ -164,6 +164,30 @@ def gated_linear_batch_invariant(input, weight, activation="gelu_tanh"):
     return out.reshape(*input.shape[:-1], f)
 
 
+def linear_residual_batch_invariant(residual, input, weight, bias=None):
+    """``residual + F.linear(input, weight, bias)`` in one GEMM whose epilogue
+    adds the residual: the linear's output is rounded to the dtype, the
+    residual added in fp32 and the sum rounded -- the bits of the two stock
+    ops, without the round trip of the linear's output through HBM.  The
+    residual stream of a transformer block (``x = x + proj(h)``) is the use.
+    Each output row depends on its own input and residual rows only, so the
+    result is batch invariant.  f16/bf16 run fused; other dtypes compose the
+    library's linear with a stock add.  Not in the reference."""
+    _require_cuda(residual, input, weight, bias)
+    assert input.shape[-1] == weight.shape[-1], "Incompatible dimensions"
+    out_shape = (*input.shape[:-1], weight.shape[0])
+    assert tuple(residual.shape) == out_shape, "residual must have the linear's output shape"
+    assert residual.dtype == input.dtype == weight.dtype, "residual, input and weight dtypes must match"
+    flat = input.reshape(-1, input.shape[-1])
+    out = None
+    if input.dtype in (torch.float16, torch.bfloat16) and flat.shape[1] > 0:
+        r2 = residual.reshape(-1, weight.shape[0])
+        out = _gemm.linear_residual(r2, flat, weight, bias)
+    if out is None:
+        return residual + linear_batch_invariant(input, weight, bias)
+    return out.reshape(out_shape)
+
+
 def bmm_batch_invariant(a, b):
     return bmm_persistent(a, b)
 

@@ -7,9 +7,11 @@ prefix keys/values of its layer and to the action tokens, integrated with a
 fixed number of flow-matching (Euler) steps over an action chunk.  Written
 with stock torch.nn.functional calls only, so that under
 ``set_batch_invariant_mode`` every GEMM, convolution, attention, softmax and
-mean runs on this library's kernels; the GeGLU input projections call the
-library's fused gated GEMM (``gated_linear_batch_invariant``) when the mode
-is on.  The weights are random (no checkpoint) and the inputs synthetic.
+mean runs on this library's kernels; when the mode is on, the GeGLU input
+projections call the library's fused gated GEMM
+(``gated_linear_batch_invariant``) and the residual adds after the output
+projections ride in the GEMM's epilogue
+(``linear_residual_batch_invariant``), with the stock ops' rounding steps.  The weights are random (no checkpoint) and the inputs synthetic.
 
 ``VLAConfig.full()`` is the BASELINE size (So400m-like 27 x 1152 vision
 tower, Gemma-2B-like 18 x 2048 prefix LM with 8 query / 1 KV heads of 256,
@@ -26,7 +28,11 @@ import math
 import torch
 import torch.nn.functional as F
 
-from .batch_invariant_ops import gated_linear_batch_invariant, is_batch_invariant_mode_enabled
+from .batch_invariant_ops import (
+    gated_linear_batch_invariant,
+    is_batch_invariant_mode_enabled,
+    linear_residual_batch_invariant,
+)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -151,9 +157,9 @@ class PiZeroStyleVLA(torch.nn.Module):
             q, k, v = F.linear(h, wqkv, bqkv).view(b, n, 3, c.vis_heads, hd).unbind(2)
             a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
                                                v.transpose(1, 2))
-            x = x + F.linear(a.transpose(1, 2).reshape(b, n, c.vis_width), wo, bo)
+            x = self._add_linear(x, a.transpose(1, 2).reshape(b, n, c.vis_width), wo, bo)
             h = F.layer_norm(x, (c.vis_width,), ln2, ln2b)
-            x = x + F.linear(F.gelu(F.linear(h, w1, b1), approximate="tanh"), w2, b2)
+            x = self._add_linear(x, F.gelu(F.linear(h, w1, b1), approximate="tanh"), w2, b2)
         x = F.layer_norm(x, (c.vis_width,), self.vis_norm, self.vis_norm_b)
         return F.linear(x, self.projector)
 
@@ -166,13 +172,22 @@ class PiZeroStyleVLA(torch.nn.Module):
         v = qkv[:, :, c.lm_heads + c.lm_kv_heads:].transpose(1, 2)
         return q, k, v
 
-    def _geglu(self, h, w_in, w_out, width):
+    @staticmethod
+    def _add_linear(r, x, w, b=None):
+        """r + F.linear(x, w, b); under the mode one GEMM with the add in its
+        epilogue (same rounding steps)."""
+        if is_batch_invariant_mode_enabled() and x.is_cuda:
+            return linear_residual_batch_invariant(r, x, w, b)
+        return r + F.linear(x, w, b)
+
+    def _geglu(self, r, h, w_in, w_out, width):
+        """r + down(gelu(gate) * up)."""
         if is_batch_invariant_mode_enabled() and h.is_cuda:
             # the library's fused GeGLU GEMM: same rounding steps as the
             # stock composition below, without the gate/up round trip to HBM
-            return F.linear(gated_linear_batch_invariant(h, w_in, "gelu_tanh"), w_out)
+            return self._add_linear(r, gated_linear_batch_invariant(h, w_in, "gelu_tanh"), w_out)
         gate, up = F.linear(h, w_in).split(width, dim=-1)
-        return F.linear(F.gelu(gate, approximate="tanh") * up, w_out)
+        return r + F.linear(F.gelu(gate, approximate="tanh") * up, w_out)
 
     def _prefix(self, image_tokens, ids):
         """Prefix LM.  Returns the final hidden state and, per layer, a joint
@@ -194,8 +209,8 @@ class PiZeroStyleVLA(torch.nn.Module):
             vbuf[:, :, :t] = v
             kv.append((kbuf, vbuf))
             a = F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
-            x = x + F.linear(a.transpose(1, 2).reshape(b, t, -1), wo)
-            x = x + self._geglu(self._rms(x, n2), w_in, w_out, c.lm_mlp)
+            x = self._add_linear(x, a.transpose(1, 2).reshape(b, t, -1), wo)
+            x = self._geglu(x, self._rms(x, n2), w_in, w_out, c.lm_mlp)
         return self._rms(x, self.lm_norm), kv
 
     def _velocity(self, xt, time, kv):
@@ -216,8 +231,8 @@ class PiZeroStyleVLA(torch.nn.Module):
             kbuf[:, :, t_pre:] = k
             vbuf[:, :, t_pre:] = v
             a = F.scaled_dot_product_attention(q, kbuf, vbuf, enable_gqa=True)
-            h = h + F.linear(a.transpose(1, 2).reshape(b, c.chunk, -1), wo)
-            h = h + self._geglu(self._rms(h, n2), w_in, w_out, c.act_mlp)
+            h = self._add_linear(h, a.transpose(1, 2).reshape(b, c.chunk, -1), wo)
+            h = self._geglu(h, self._rms(h, n2), w_in, w_out, c.act_mlp)
         return F.linear(self._rms(h, self.act_norm), self.act_out)
 
     def forward(self, images, ids, noise):

@@ -288,7 +288,8 @@ namespace {
 
 // Shared body of bio_gemm / bio_gemm_tiled; `forced` (when non-null) replaces
 // the library's tile choice for the tensor-core path.
-int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v) {
+int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v,
+              const EpiResidual* res = nullptr) {
   if (a == nullptr) return BIO_ERR_ARG;
   if ((a->flags & ~BIO_GEMM_BIAS_PER_ROW) != 0) return BIO_ERR_ARG;
   if (a->m < 0 || a->n < 0 || a->k < 0 || a->batch1 < 0 || a->batch2 < 1) return BIO_ERR_SHAPE;
@@ -340,8 +341,9 @@ int gemm_impl(const bio_gemm_args* a, const TileChoice* forced, void* stream_v) 
   // An N-contiguous B is staged in 64-column swizzle atoms: tiles narrower
   // than one atom are not built for it.
   if (b_mn && !tc.pair && (tc.bn < 64 || tc.bn == 96)) return BIO_ERR_ARG;
-  if (a->dtype == BIO_BF16) return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn);
-  return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn);
+  if (a->dtype == BIO_BF16)
+    return dispatch_tc<__nv_bfloat16>(a, tc, stream, a_mn, b_mn, nullptr, nullptr, nullptr, res);
+  return dispatch_tc<__half>(a, tc, stream, a_mn, b_mn, nullptr, nullptr, nullptr, res);
 }
 
 template <typename T>
@@ -411,6 +413,17 @@ int grouped_impl(const bio_gemm_args* a, const int32_t* seg, const void* up, voi
 extern "C" {
 
 int bio_gemm(const bio_gemm_args* a, void* stream_v) { return gemm_impl(a, nullptr, stream_v); }
+
+int bio_gemm_residual(const bio_gemm_args* a, const void* residual, int64_t residual_row_stride,
+                      void* stream_v) {
+  if (a == nullptr || residual == nullptr) return BIO_ERR_ARG;
+  if (a->dtype != BIO_F16 && a->dtype != BIO_BF16) return BIO_ERR_DTYPE;
+  if (a->batch1 != 1 || a->batch2 != 1 || a->flags != 0) return BIO_ERR_ARG;
+  if (a->k < 1) return BIO_ERR_SHAPE;
+  if (a->c_sn != 1 || residual_row_stride < a->n) return BIO_ERR_STRIDE;
+  const EpiResidual res{residual, residual_row_stride};
+  return gemm_impl(a, nullptr, stream_v, &res);
+}
 
 int bio_gemm_tiled(const bio_gemm_args* a, int32_t tile_m, int32_t tile_n, void* stream_v) {
   if (tile_m != 128 && tile_m != 256) return BIO_ERR_ARG;

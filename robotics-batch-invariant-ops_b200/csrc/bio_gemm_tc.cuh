@@ -61,6 +61,11 @@ struct TcGemmParams {
   float alpha;
   int c_vec_ok;
   int* status;
+  // residual mode (plain 2-D GEMM): C = round(alpha A B + bias) + R, rounded
+  // again -- the rounding chain of a linear followed by an add; R is
+  // row-contiguous with r_sm elements between rows
+  const void* resid;
+  int64_t r_sm;
 };
 
 struct TileIdx {
@@ -381,6 +386,28 @@ __device__ __forceinline__ void epi_add_bias(float (&v)[32], bool has, bool per_
   }
 }
 
+// Residual mode: the chunk's outputs are rounded to the dtype (the GEMM's own
+// rounding), then R[m, n0 .. n0+31] is added in fp32; the store rounds again.
+template <typename T>
+__device__ __forceinline__ void epi_add_resid(const TcGemmParams& p, float (&v)[32], int m,
+                                              int rows, int n0) {
+  if (m >= rows || n0 >= p.n) return;
+  const T* rr = static_cast<const T*>(p.resid) + static_cast<int64_t>(m) * p.r_sm + n0;
+  if (n0 + 32 <= p.n && (reinterpret_cast<uintptr_t>(rr) & 15u) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = reinterpret_cast<const uint4*>(rr)[q];
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[8 * q + i] = round_to<T>(v[8 * q + i]) + to_f32(e[i]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = round_to<T>(v[j]) + (n0 + j < p.n ? to_f32(rr[j]) : 0.f);
+  }
+}
+
 // One 32-column chunk of an accumulator row (TMEM words r) of output row m:
 // alpha, then the transposed-convolution scatter, or bias (per column, or
 // per row with BIAS_PER_ROW; prefetched, see EpiBias) and one rounding,
@@ -399,6 +426,7 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const uint32_t 
     return;
   }
   epi_add_bias(v, has_bias, p.bias_per_row != 0, bcol, brow);
+  if (p.resid != nullptr) epi_add_resid<T>(p, v, m, rows, n0);
   if (m >= rows || n0 >= p.n) return;
   if (p.c_vec_ok && n0 + 32 <= p.n) {
     uint4* dst = reinterpret_cast<uint4*>(crow + n0);
@@ -426,11 +454,12 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const uint32_t 
 template <typename T>
 __device__ __forceinline__ void epi_chunk_stage(const TcGemmParams& p, const uint32_t (&r)[32],
                                                 uint8_t* stage, bool has_bias, float bcol,
-                                                float brow, int lane) {
+                                                float brow, int lane, int m, int rows, int n0) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
   epi_add_bias(v, has_bias, p.bias_per_row != 0, bcol, brow);
+  if (p.resid != nullptr) epi_add_resid<T>(p, v, m, rows, n0);
   uint8_t* row = stage + lane * 64;
   const int sw = (lane >> 1) & 3;
 #pragma unroll
@@ -466,7 +495,7 @@ __device__ __forceinline__ void epi_tile(const TcGemmParams& p, const CUtensorMa
         if (lane == 0) bulk_wait_read<NBUF - 1>();
         __syncwarp();
       }
-      epi_chunk_stage<T>(p, rr, buf, eb.has, bcol, eb.row, lane);
+      epi_chunk_stage<T>(p, rr, buf, eb.has, bcol, eb.row, lane, m, rows, n0);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -1314,9 +1343,16 @@ struct ScatterSpec {
   bool vec;
 };
 
+// Residual operand of bio_gemm_residual (see TcGemmParams::resid).
+struct EpiResidual {
+  const void* ptr;
+  int64_t row_stride;
+};
+
 template <bool PAIR, int BN, bool A_MN, bool B_MN, typename T>
 int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
-              const void* b_up = nullptr, const ScatterSpec* sc = nullptr) {
+              const void* b_up = nullptr, const ScatterSpec* sc = nullptr,
+              const EpiResidual* res = nullptr) {
   constexpr int STAGES = stages_for<PAIR, BN>();
   constexpr uint32_t kSmem = smem_bytes<PAIR, BN, STAGES>();
   constexpr int kTileM = PAIR ? 256 : kBM;        // rows of C per tile
@@ -1414,6 +1450,8 @@ int launch_tc(const bio_gemm_args* a, const int* seg, cudaStream_t stream,
   p.tiles_n = static_cast<int>((a->n + out_bn - 1) / out_bn);
   p.swiglu = b_up == nullptr ? 0 : ((a->flags & BIO_GEMM_GATE_GELU_TANH) ? 2 : 1);
   p.scatter = 0;
+  p.resid = res != nullptr ? res->ptr : nullptr;
+  p.r_sm = res != nullptr ? res->row_stride : 0;
   if (sc != nullptr) {
     p.scatter = 1;
     p.sc_s1 = sc->s1;
@@ -1552,28 +1590,29 @@ inline bool tile_supported(const TileChoice& tc) {
 // translation unit (bio_gemm_tc_*.cu) so the kernels compile in parallel.
 template <bool A_MN, bool B_MN, typename T>
 int dispatch_bn(const bio_gemm_args* a, const TileChoice& tc, const int* seg,
-                cudaStream_t stream, const ScatterSpec* sc, const void* b_up) {
+                cudaStream_t stream, const ScatterSpec* sc, const void* b_up,
+                const EpiResidual* res) {
   if (tc.pair) {
-    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
-    return launch_tc<true, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    if (tc.bn == 128) return launch_tc<true, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
+    return launch_tc<true, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
   }
   switch (tc.bn) {
-    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
-    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+    case 32: return launch_tc<false, 32, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
+    case 64: return launch_tc<false, 64, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
     case 96:
       // 96 columns are not a whole number of 64-column atoms of an
       // N-contiguous B
       if constexpr (B_MN) return BIO_ERR_ARG;
-      else return launch_tc<false, 96, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
-    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
-    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc);
+      else return launch_tc<false, 96, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
+    case 128: return launch_tc<false, 128, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
+    default: return launch_tc<false, 256, A_MN, B_MN, T>(a, seg, stream, b_up, sc, res);
   }
 }
 
 #define BIO_GEMM_TC_DECL(KW, A_MN, B_MN, T)                                                   \
   KW template int dispatch_bn<A_MN, B_MN, T>(const bio_gemm_args*, const TileChoice&,       \
                                              const int*, cudaStream_t, const ScatterSpec*, \
-                                             const void*);
+                                             const void*, const EpiResidual*);
 BIO_GEMM_TC_DECL(extern, false, false, __nv_bfloat16)
 BIO_GEMM_TC_DECL(extern, false, true, __nv_bfloat16)
 BIO_GEMM_TC_DECL(extern, true, false, __nv_bfloat16)
@@ -1586,13 +1625,13 @@ BIO_GEMM_TC_DECL(extern, true, true, __half)
 template <typename T>
 int dispatch_tc(const bio_gemm_args* a, const TileChoice& tc, cudaStream_t stream, bool a_mn,
                 bool b_mn, const int* seg = nullptr, const ScatterSpec* sc = nullptr,
-                const void* b_up = nullptr) {
+                const void* b_up = nullptr, const EpiResidual* res = nullptr) {
   if (a_mn) {
-    return b_mn ? dispatch_bn<true, true, T>(a, tc, seg, stream, sc, b_up)
-                : dispatch_bn<true, false, T>(a, tc, seg, stream, sc, b_up);
+    return b_mn ? dispatch_bn<true, true, T>(a, tc, seg, stream, sc, b_up, res)
+                : dispatch_bn<true, false, T>(a, tc, seg, stream, sc, b_up, res);
   }
-  return b_mn ? dispatch_bn<false, true, T>(a, tc, seg, stream, sc, b_up)
-              : dispatch_bn<false, false, T>(a, tc, seg, stream, sc, b_up);
+  return b_mn ? dispatch_bn<false, true, T>(a, tc, seg, stream, sc, b_up, res)
+              : dispatch_bn<false, false, T>(a, tc, seg, stream, sc, b_up, res);
 }
 
 }  // namespace bio_gemm_tc
