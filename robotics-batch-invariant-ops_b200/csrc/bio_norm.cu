@@ -122,7 +122,7 @@ __device__ __forceinline__ void param8(const W* p, int base, int n, float fill, 
 
 // Row held in registers: GPT (groups per thread) groups of 8 per thread.
 template <typename T, typename W, int TEAM, int GPT, bool RMS>
-__global__ void __launch_bounds__(TEAM == 32 ? 256 : TEAM)
+__global__ void __launch_bounds__(TEAM == 32 ? 256 : TEAM, (TEAM == 32 && RMS && GPT == 8) ? 3 : 1)
     norm_reg_kernel(const NormParams p) {
   __shared__ float red[32];
   const int lane_in_team = TEAM == 32 ? (threadIdx.x & 31) : threadIdx.x;
