@@ -122,7 +122,13 @@ __device__ __forceinline__ void param8(const W* p, int base, int n, float fill, 
 
 // Row held in registers: GPT (groups per thread) groups of 8 per thread.
 template <typename T, typename W, int TEAM, int GPT, bool RMS>
-__global__ void __launch_bounds__(TEAM == 32 ? 256 : TEAM, (TEAM == 32 && RMS && GPT == 8) ? 3 : 1)
+// One-warp teams: 8 rows per 256-thread CTA, and enough CTAs per SM to keep
+// rows in flight.  Three CTAs cap a thread at 80 registers, which holds the
+// 16-bit RMSNorm rows and LayerNorm rows of up to 5 groups without spills;
+// the rest keep two CTAs (128 registers).
+__global__ void __launch_bounds__(
+    TEAM == 32 ? 256 : TEAM,
+    TEAM == 32 ? ((sizeof(T) == 2 && sizeof(W) == 2 && (RMS || GPT <= 5)) ? 3 : 2) : 1)
     norm_reg_kernel(const NormParams p) {
   __shared__ float red[32];
   const int lane_in_team = TEAM == 32 ? (threadIdx.x & 31) : threadIdx.x;
@@ -271,6 +277,9 @@ int launch_norm(const bio::NormParams& p, cudaStream_t s) {
     bio::norm_reg_kernel<T, W, 32, 2, RMS><<<warp_blocks, 256, 0, s>>>(p);
   } else if (n <= 1024) {
     bio::norm_reg_kernel<T, W, 32, 4, RMS><<<warp_blocks, 256, 0, s>>>(p);
+  } else if (n <= 1280) {
+    // e.g. the 1152-wide vision rows: five groups of 8 per lane
+    bio::norm_reg_kernel<T, W, 32, 5, RMS><<<warp_blocks, 256, 0, s>>>(p);
   } else if (n <= bio::kNormWarpMax) {
     bio::norm_reg_kernel<T, W, 32, 8, RMS><<<warp_blocks, 256, 0, s>>>(p);
   } else if (n <= 4096) {
